@@ -1,0 +1,180 @@
+// unpermute.cu -- fused weighted unpermute + top-K combine for sm_100a.
+//
+//   out[t, :] = round16( sum_{k<K} w[p_k] * y[p_k, :] ),  p_k = slot_pos[t*K + k]
+//
+// Replaces the reference's unpack_combine_kernel (fp32 atomicAdd scatter into
+// a zeroed [T, d] fp32 buffer, apps/bench_e2e.cu:136-147) plus its separate
+// f32_to_f16_kernel pass (:149-152) and memset (:304).  Here each token
+// GATHERS its K rows, so there are no atomics, no fp32 round trip through
+// HBM, and the sum is deterministic: fp32, ascending k, one FMA per term.
+// HBM traffic is the algorithmic minimum: T*K*d*2 bytes read + T*d*2 written.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace moe_b200 {
+
+template <int DT>
+__device__ __forceinline__ void acc_vec(float (&a)[8], float w, const uint4& v) {
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+        float2 f;
+        if (DT == MOE_B200_F16) {
+            __half2 x = *reinterpret_cast<const __half2*>(&u[h]);
+            f = __half22float2(x);
+        } else {
+            __nv_bfloat162 x = *reinterpret_cast<const __nv_bfloat162*>(&u[h]);
+            f = __bfloat1622float2(x);
+        }
+        a[2 * h] = __fmaf_rn(w, f.x, a[2 * h]);
+        a[2 * h + 1] = __fmaf_rn(w, f.y, a[2 * h + 1]);
+    }
+}
+
+template <int DT>
+__device__ __forceinline__ uint4 pack_vec(const float (&a)[8]) {
+    uint32_t u[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+        if (DT == MOE_B200_F16) {
+            __half2 x = __floats2half2_rn(a[2 * h], a[2 * h + 1]);
+            u[h] = *reinterpret_cast<uint32_t*>(&x);
+        } else {
+            __nv_bfloat162 x = __floats2bfloat162_rn(a[2 * h], a[2 * h + 1]);
+            u[h] = *reinterpret_cast<uint32_t*>(&x);
+        }
+    }
+    return make_uint4(u[0], u[1], u[2], u[3]);
+}
+
+// One warp per token.  VPL 16-byte vectors per lane per pass; the K source
+// rows are fetched KB at a time so that KB*VPL loads are in flight per lane.
+template <int DT, int VPL, int KB>
+__global__ void __launch_bounds__(256)
+unpermute_kernel(const uint4* __restrict__ y, const float* __restrict__ packed_w,
+                 const int32_t* __restrict__ slot_pos, int T, int K, int nvec,
+                 uint4* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int warps_per_cta = blockDim.x >> 5;
+    const int64_t gw = int64_t(blockIdx.x) * warps_per_cta + (threadIdx.x >> 5);
+    const int64_t nw = int64_t(gridDim.x) * warps_per_cta;
+
+    for (int64_t t = gw; t < T; t += nw) {
+        int32_t p_lane = lane < K ? __ldg(slot_pos + t * K + lane) : -1;
+        float w_lane = p_lane >= 0 ? __ldg(packed_w + p_lane) : 0.f;
+        for (int c0 = 0; c0 < nvec; c0 += 32 * VPL) {
+            float acc[VPL][8];
+#pragma unroll
+            for (int j = 0; j < VPL; ++j)
+#pragma unroll
+                for (int h = 0; h < 8; ++h) acc[j][h] = 0.f;
+
+            for (int kb = 0; kb < K; kb += KB) {
+                uint4 v[KB][VPL];
+                int32_t p[KB];
+#pragma unroll
+                for (int q = 0; q < KB; ++q) {
+                    p[q] = __shfl_sync(0xffffffffu, p_lane, (kb + q) & 31);
+                    if (kb + q >= K) p[q] = -1;
+#pragma unroll
+                    for (int j = 0; j < VPL; ++j) {
+                        int i = c0 + j * 32 + lane;
+                        if (p[q] >= 0 && i < nvec) v[q][j] = ld_nc_v4(y + int64_t(p[q]) * nvec + i);
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < KB; ++q) {
+                    float w = __shfl_sync(0xffffffffu, w_lane, (kb + q) & 31);
+                    if (p[q] < 0) continue;
+#pragma unroll
+                    for (int j = 0; j < VPL; ++j) acc_vec<DT>(acc[j], w, v[q][j]);
+                }
+            }
+            uint4* dst = out + t * nvec;
+#pragma unroll
+            for (int j = 0; j < VPL; ++j) {
+                int i = c0 + j * 32 + lane;
+                if (i < nvec) st_v4(dst + i, pack_vec<DT>(acc[j]));
+            }
+        }
+    }
+}
+
+// Fallback for rows that are not 16-byte multiples / not 16-byte aligned.
+template <int DT>
+__global__ void __launch_bounds__(256)
+unpermute_scalar_kernel(const uint16_t* __restrict__ y, const float* __restrict__ packed_w,
+                        const int32_t* __restrict__ slot_pos, int T, int K, int d,
+                        uint16_t* __restrict__ out) {
+    const int64_t n = int64_t(T) * d;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += int64_t(gridDim.x) * blockDim.x) {
+        int64_t t = i / d, c = i % d;
+        float a = 0.f;
+        for (int k = 0; k < K; ++k) {
+            int32_t p = slot_pos[t * K + k];
+            if (p < 0) continue;
+            uint16_t raw = y[int64_t(p) * d + c];
+            float f;
+            if (DT == MOE_B200_F16) f = __half2float(*reinterpret_cast<const __half*>(&raw));
+            else f = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(&raw));
+            a = __fmaf_rn(packed_w[p], f, a);
+        }
+        if (DT == MOE_B200_F16) {
+            __half h = __float2half_rn(a);
+            out[i] = *reinterpret_cast<uint16_t*>(&h);
+        } else {
+            __nv_bfloat16 h = __float2bfloat16_rn(a);
+            out[i] = *reinterpret_cast<uint16_t*>(&h);
+        }
+    }
+}
+
+static int sm_count_unperm() {
+    int dev = 0, n = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+cudaError_t launch_unpermute(const void* y, const float* packed_w, const int32_t* slot_pos,
+                             int T, int K, int d, int dtype, void* out, cudaStream_t stream) {
+    const bool vec = (d % 8 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(out) % 16 == 0);
+    const int threads = 256;
+    if (vec) {
+        const int warps_per_cta = threads / 32;
+        int64_t want = (int64_t(T) + warps_per_cta - 1) / warps_per_cta;
+        int64_t cap = int64_t(sm_count_unperm()) * 64;
+        int grid = int(want < cap ? want : cap);
+        if (grid < 1) grid = 1;
+        if (dtype == MOE_B200_F16)
+            unpermute_kernel<MOE_B200_F16, 2, 4><<<grid, threads, 0, stream>>>(
+                static_cast<const uint4*>(y), packed_w, slot_pos, T, K, d / 8,
+                static_cast<uint4*>(out));
+        else
+            unpermute_kernel<MOE_B200_BF16, 2, 4><<<grid, threads, 0, stream>>>(
+                static_cast<const uint4*>(y), packed_w, slot_pos, T, K, d / 8,
+                static_cast<uint4*>(out));
+    } else {
+        int64_t n = int64_t(T) * d;
+        int64_t want = (n + threads - 1) / threads;
+        int64_t cap = int64_t(sm_count_unperm()) * 32;
+        int grid = int(want < cap ? want : cap);
+        if (grid < 1) grid = 1;
+        if (dtype == MOE_B200_F16)
+            unpermute_scalar_kernel<MOE_B200_F16><<<grid, threads, 0, stream>>>(
+                static_cast<const uint16_t*>(y), packed_w, slot_pos, T, K, d,
+                static_cast<uint16_t*>(out));
+        else
+            unpermute_scalar_kernel<MOE_B200_BF16><<<grid, threads, 0, stream>>>(
+                static_cast<const uint16_t*>(y), packed_w, slot_pos, T, K, d,
+                static_cast<uint16_t*>(out));
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace moe_b200

@@ -1,0 +1,115 @@
+/*
+ * moe_b200.h -- C ABI of libmoe_b200, the sm_100a MoE token packing and
+ * dispatch library.
+ *
+ * Conventions
+ *  - Every pointer argument is a device pointer unless its comment says
+ *    "host".  All device buffers are owned by the caller.
+ *  - Token rows are opaque 16-bit words (fp16 or bf16); `dtype` matters only
+ *    where arithmetic happens (combine, FFN): MOE_B200_F16 or MOE_B200_BF16.
+ *  - `stream` is a cudaStream_t (NULL = the legacy default stream).  Work is
+ *    enqueued asynchronously; no entry point blocks the host unless its
+ *    comment says so.
+ *  - Return value: MOE_B200_OK or a host-detected error (bad argument, short
+ *    workspace, CUDA launch failure).  Errors the device detects while running
+ *    (an assignment outside [0, E), a bounded wait that ran out) are recorded
+ *    in the workspace and read with moe_b200_workspace_status().
+ *
+ * Reference interfaces replaced (paths within feiyang-cmu/15618-final):
+ *  - moe_b200_pack* replace moe::IScatter::workspace_bytes / run
+ *    (include/moe/scatter.cuh:37, :48-53) and the strategies behind them
+ *    (src/scatter/scatter_{atomic,sort,warp,vec,csort}.cu); the output
+ *    contract is moe::cpu_scatter's (src/common/cpu_reference.cpp:12-51).
+ *  - moe_b200_unpermute replaces the app-local unpack_combine_kernel +
+ *    f32_to_f16_kernel pair (apps/bench_e2e.cu:136-152, launched :304-312).
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum moe_b200_status {
+    MOE_B200_OK = 0,
+    MOE_B200_ERR_INVALID_ARG = 1,      /* bad size, null pointer, misaligned */
+    MOE_B200_ERR_WORKSPACE = 2,        /* workspace null or too small */
+    MOE_B200_ERR_UNSUPPORTED = 3,      /* shape outside the supported limits */
+    MOE_B200_ERR_CUDA = 4,             /* a CUDA call or launch failed */
+    /* device-side conditions, reported by moe_b200_workspace_status() as bits */
+    MOE_B200_DEV_BAD_ASSIGNMENT = 0x10, /* some assignment was outside [0, E) */
+    MOE_B200_DEV_WAIT_TIMEOUT = 0x20    /* a bounded cross-CTA wait gave up */
+};
+
+enum moe_b200_dtype { MOE_B200_F16 = 0, MOE_B200_BF16 = 1 };
+
+/* Limits of the packing kernels. */
+#define MOE_B200_MAX_EXPERTS 1024
+
+/* Library version (major*10000 + minor*100 + patch). */
+int moe_b200_version(void);
+
+/* Static description of a status code. */
+const char* moe_b200_status_string(int status);
+
+/* Human-readable text of the last host-side error on this thread ("" if none). */
+const char* moe_b200_last_error(void);
+
+/* ---------------------------------------------------------------- pack ---- */
+
+/* Scratch bytes moe_b200_pack needs for T tokens, K slots each, E experts.
+ * Replaces moe::IScatter::workspace_bytes (include/moe/scatter.cuh:37).     */
+size_t moe_b200_pack_workspace_bytes(int T, int K, int E);
+
+/* Zero-fill a workspace before its first use (enqueued on `stream`).  Every
+ * moe_b200_pack call leaves the workspace zero-filled again, so this is needed
+ * once per allocation, not per call.                                        */
+int moe_b200_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+
+/* Pack token rows by expert, stably: within each expert the rows keep
+ * ascending (t, k) order, exactly as moe::cpu_scatter
+ * (src/common/cpu_reference.cpp:12-51) produces them.  Replaces
+ * moe::IScatter::run (include/moe/scatter.cuh:48-53).
+ *   emb            [T, d]    16-bit rows (read only)
+ *   asgn           [T, K]    expert of slot (t, k), in [0, E)
+ *   wts            [T, K]    routing weight of slot (t, k); may be NULL when
+ *                            packed_weights is NULL
+ *   packed         [T*K, d]  out: packed[p] = emb[perm[p]]
+ *   packed_weights [T*K]     out: weight of packed row p (may be NULL)
+ *   perm           [T*K]     out: source token of packed row p
+ *   expert_count   [E]       out: rows per expert
+ *   expert_start   [E+1]     out: exclusive prefix of expert_count; [E] = T*K
+ *   slot_pos       [T*K]     out (may be NULL): packed row of slot (t, k), the
+ *                            inverse of perm that moe_b200_unpermute reads
+ *   workspace      moe_b200_pack_workspace_bytes(T, K, E) bytes, zero-filled
+ *                  once with moe_b200_workspace_init.
+ * Concurrent calls must use distinct workspaces.                            */
+int moe_b200_pack(const void* emb, const int32_t* asgn, const float* wts,
+                  int T, int K, int E, int d,
+                  void* packed, float* packed_weights, int32_t* perm,
+                  int32_t* expert_count, int32_t* expert_start, int32_t* slot_pos,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Synchronise `stream`, then read and clear the device-side condition bits
+ * (MOE_B200_DEV_*) recorded in `workspace`; *device_status = 0 means clean. */
+int moe_b200_workspace_status(void* workspace, size_t workspace_bytes, void* stream,
+                              int* device_status /* host */);
+
+/* ------------------------------------------------------------ combine ---- */
+
+/* Weighted unpermute + top-K combine:
+ *   out[t, :] = round16( sum_{k=0..K-1} packed_weights[p] * y[p, :] ),
+ *   p = slot_pos[t*K + k],  accumulated in fp32 in ascending k.
+ * Replaces unpack_combine_kernel + f32_to_f16_kernel (apps/bench_e2e.cu:136-152).
+ *   y [T*K, d] 16-bit expert outputs in packed order; out [T, d] 16-bit.    */
+int moe_b200_unpermute(const void* y, const float* packed_weights, const int32_t* slot_pos,
+                       int T, int K, int d, int dtype, void* out, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* MOE_B200_H */

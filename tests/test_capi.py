@@ -1,0 +1,94 @@
+"""CPU tests of the C-ABI library: it loads, exports every entry point that
+include/moe_b200.h declares (plus the C++ IScatter boundary), and rejects
+bad arguments on the host before touching a GPU."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+import moe_b200 as mb
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "moe_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(moe_b200_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = mb.lib()
+    names = declared_functions()
+    assert len(names) >= 7
+    for n in names:
+        assert hasattr(L, n), n
+
+
+def test_cpp_boundary_symbols_exported():
+    out = subprocess.check_output(["nm", "-D", "--defined-only", mb.LIB_PATH], text=True)
+    demangled = subprocess.check_output(["c++filt"], input=out, text=True)
+    assert "moe::make_scatter(std::__cxx11::basic_string" in demangled
+    assert "moe::make_b200_scatter()" in demangled
+
+
+def test_version_and_status_strings():
+    L = mb.lib()
+    assert L.moe_b200_version() >= 100
+    assert L.moe_b200_status_string(0) == b"ok"
+    assert b"argument" in L.moe_b200_status_string(1)
+
+
+def test_workspace_bytes():
+    a = mb.pack_workspace_bytes(8192, 4, 60)
+    assert a >= 8192 * 4 * 4 + 256
+    assert a % 256 == 0
+    assert mb.pack_workspace_bytes(65536, 8, 128) > a
+    assert mb.pack_workspace_bytes(-1, 4, 60) == 0
+    assert mb.pack_workspace_bytes(10, 0, 60) == 0
+
+
+def _pack(T=16, K=2, E=4, d=8, ws=0x1000, ws_bytes=1 << 20, dev=0x2000):
+    L = mb.lib()
+    return L.moe_b200_pack(dev, dev, dev, T, K, E, d, dev, dev, dev, dev, dev, None, ws, ws_bytes, None)
+
+
+def test_pack_rejects_bad_arguments_on_host():
+    assert _pack(T=-1) == mb.ERR_INVALID_ARG
+    assert _pack(K=0) == mb.ERR_INVALID_ARG
+    assert _pack(E=0) == mb.ERR_INVALID_ARG
+    assert _pack(d=0) == mb.ERR_INVALID_ARG
+    assert _pack(K=33) == mb.ERR_UNSUPPORTED
+    assert _pack(E=mb.MAX_EXPERTS + 1) == mb.ERR_UNSUPPORTED
+    assert _pack(T=1 << 30, K=4) == mb.ERR_UNSUPPORTED
+    assert _pack(ws_bytes=8) == mb.ERR_WORKSPACE
+    assert _pack(ws=0) == mb.ERR_WORKSPACE
+    assert _pack(ws=0x1010) == mb.ERR_INVALID_ARG  # not 256-byte aligned
+    assert b"workspace" in mb.lib().moe_b200_last_error()
+
+
+def test_unpermute_rejects_bad_arguments_on_host():
+    L = mb.lib()
+    p = 0x2000
+    assert L.moe_b200_unpermute(p, p, p, 4, 2, 8, 7, p, None) == mb.ERR_INVALID_ARG
+    assert L.moe_b200_unpermute(p, p, p, -1, 2, 8, 0, p, None) == mb.ERR_INVALID_ARG
+    assert L.moe_b200_unpermute(p, p, p, 4, 40, 8, 0, p, None) == mb.ERR_UNSUPPORTED
+    assert L.moe_b200_unpermute(None, p, p, 4, 2, 8, 0, p, None) == mb.ERR_INVALID_ARG
+    assert L.moe_b200_unpermute(p, p, p, 0, 2, 8, 0, p, None) == mb.OK  # empty: no-op
+
+
+def test_python_boundary_mirrors_reference_factory():
+    assert mb.make_scatter("nope") is None
+    s = mb.make_scatter("b200")
+    assert s.name() == "b200"
+    p = mb.MoEParams(T=2048, K=4, E=64, d_model=2048)
+    assert s.workspace_bytes(p) == mb.pack_workspace_bytes(2048, 4, 64)
+
+
+def test_errors_raise():
+    with pytest.raises(mb.MoEB200Error) as ei:
+        mb._check(mb.ERR_WORKSPACE, "x")
+    assert ei.value.status == mb.ERR_WORKSPACE

@@ -1,0 +1,158 @@
+"""CPU tests of the oracle: pinned against the reference's own cpu_scatter
+outputs (golden vectors in tests/golden, made by tests/golden/make_golden.py),
+and the conversion / combine / FFN restatements against independent numpy and
+torch computations."""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import GOLDEN
+
+GOLDEN_FILES = sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
+
+
+def test_golden_files_present():
+    names = {os.path.basename(f) for f in GOLDEN_FILES}
+    assert "verify_mini.npz" in names
+    assert sum(n.startswith("fixture_") for n in names) == 6
+
+
+@pytest.mark.parametrize("path", GOLDEN_FILES, ids=os.path.basename)
+def test_oracle_scatter_matches_reference_golden(path):
+    g = np.load(path)
+    E = int(g["E"])
+    asgn, wts = g["asgn"], g["wts"]
+    T = asgn.shape[0]
+    emb = g["emb"] if "emb" in g else np.zeros((T, 8), np.uint16)
+    r = oracle.scatter(emb, asgn, wts, E)
+    np.testing.assert_array_equal(r["perm"], g["perm"])
+    np.testing.assert_array_equal(r["expert_start"][:E], g["expert_start"])
+    np.testing.assert_array_equal(r["expert_count"], g["expert_count"])
+    assert r["expert_start"][E] == asgn.size
+    assert r["packed_weights"].tobytes() == g["packed_weights"].tobytes()
+    if "packed" in g:
+        assert r["packed"].tobytes() == g["packed"].tobytes()
+    # slot_pos is the inverse of perm
+    sp = r["slot_pos"]
+    assert np.array_equal(r["perm"][sp], np.repeat(np.arange(T), asgn.shape[1]))
+    assert oracle.verify(emb, asgn, wts, r["packed"], r["packed_weights"], r["expert_start"],
+                         r["expert_count"], r["perm"], E) == 0
+
+
+def test_verify_detects_planted_errors():
+    g = np.load(os.path.join(GOLDEN, "fixture_syn_zipf_T512.npz"))
+    E = int(g["E"])
+    emb, asgn, wts = g["emb"], g["asgn"], g["wts"]
+    r = oracle.scatter(emb, asgn, wts, E)
+    args = lambda **kw: dict(dict(packed=r["packed"], packed_w=r["packed_weights"],
+                                  expert_start=r["expert_start"], expert_count=r["expert_count"],
+                                  perm=r["perm"]), **kw)
+    assert oracle.verify(emb, asgn, wts, E=E, **args()) == 0
+    bad = r["packed"].copy(); bad[5, 3] ^= 1
+    assert oracle.verify(emb, asgn, wts, E=E, **args(packed=bad)) > 0
+    badw = r["packed_weights"].copy(); badw[7] += 1.0
+    assert oracle.verify(emb, asgn, wts, E=E, **args(packed_w=badw)) > 0
+    badc = r["expert_count"].copy(); badc[0] += 1; badc[1] -= 1
+    assert oracle.verify(emb, asgn, wts, E=E, **args(expert_count=badc)) > 0
+    badp = r["perm"].copy(); badp[0], badp[-1] = badp[-1], badp[0]
+    assert oracle.verify(emb, asgn, wts, E=E, **args(perm=badp)) > 0
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="reference CPU oracle not built")
+@pytest.mark.parametrize("T,K,E,d,seed", [(1, 1, 1, 8, 0), (37, 3, 5, 24, 1), (300, 4, 60, 64, 2),
+                                          (1000, 8, 128, 16, 3), (5, 2, 1000, 8, 4)])
+def test_oracle_matches_reference_binary_random(T, K, E, d, seed):
+    rng = np.random.default_rng(seed)
+    emb = rng.integers(0, 65536, size=(T, d), dtype=np.uint16)
+    asgn = np.stack([rng.choice(E, K, replace=K > E) for _ in range(T)]).astype(np.int32)
+    wts = rng.random((T, K), dtype=np.float32)
+    a = oracle.scatter(emb, asgn, wts, E)
+    b = oracle.ref_scatter(emb, asgn, wts, E)
+    for key in ("packed", "packed_weights", "perm", "expert_count"):
+        assert a[key].tobytes() == b[key].tobytes(), key
+    np.testing.assert_array_equal(a["expert_start"][:E], b["expert_start"])
+
+
+def test_scatter_rejects_bad_assignment():
+    with pytest.raises(ValueError):
+        oracle.scatter(np.zeros((2, 8), np.uint16), np.array([[0], [3]], np.int32), None, 3)
+
+
+def test_f16_conversion_matches_numpy():
+    rng = np.random.default_rng(0)
+    x = np.concatenate([
+        rng.standard_normal(200000).astype(np.float32) * np.float32(10.0) ** rng.integers(-9, 5, 200000),
+        np.array([0.0, -0.0, 65504.0, 65519.99, 65520.0, 1e-8, 5.96e-8, 2.98e-8, -3e-8, np.inf, -np.inf],
+                 np.float32),
+    ]).astype(np.float32)
+    got = oracle.f32_to_16(x, 0)
+    want = x.astype(np.float16).view(np.uint16)
+    np.testing.assert_array_equal(got, want)
+    allh = np.arange(65536, dtype=np.uint16)
+    finite = ~np.isnan(allh.view(np.float16))
+    np.testing.assert_array_equal(oracle.to_f32(allh, 0)[finite], allh.view(np.float16)[finite].astype(np.float32))
+
+
+def test_bf16_conversion_matches_torch():
+    import torch
+    rng = np.random.default_rng(1)
+    x = (rng.standard_normal(200000) * 10.0 ** rng.integers(-30, 30, 200000)).astype(np.float32)
+    got = oracle.f32_to_16(x, 1)
+    want = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    np.testing.assert_array_equal(got, want)
+    allb = np.arange(65536, dtype=np.uint16)
+    ref = torch.from_numpy(allb.view(np.int16)).view(torch.bfloat16).float().numpy()
+    finite = ~np.isnan(ref)
+    np.testing.assert_array_equal(oracle.to_f32(allb, 1)[finite], ref[finite])
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_combine_identity_expert_closed_form(dtype):
+    """y = packed rows (identity expert): out[t] = round16(sum_k w[t,k] * emb[t])."""
+    rng = np.random.default_rng(2)
+    T, K, E, d = 64, 4, 8, 32
+    embf = rng.standard_normal((T, d)).astype(np.float32)
+    emb = oracle.f32_to_16(embf, dtype)
+    asgn = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+    wts = rng.random((T, K)).astype(np.float32)
+    r = oracle.scatter(emb, asgn, wts, E)
+    out = oracle.combine(r["packed"], r["packed_weights"], r["slot_pos"], T, K, dtype)
+    x = oracle.to_f32(emb, dtype)
+    acc = np.zeros((T, d), np.float32)
+    for k in range(K):
+        acc = (wts[:, k:k + 1].astype(np.float64) * x + acc).astype(np.float32)  # fma-exact enough
+    np.testing.assert_allclose(oracle.to_f32(out, dtype), acc, rtol=1e-2 if dtype else 1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_combine_agrees_with_reference_order(dtype):
+    rng = np.random.default_rng(3)
+    T, K, E, d = 100, 4, 10, 40
+    emb = oracle.f32_to_16(rng.standard_normal((T, d)).astype(np.float32), dtype)
+    asgn = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+    wts = rng.random((T, K)).astype(np.float32)
+    r = oracle.scatter(emb, asgn, wts, E)
+    y = oracle.f32_to_16(rng.standard_normal((T * K, d)).astype(np.float32), dtype)
+    a = oracle.to_f32(oracle.combine(y, r["packed_weights"], r["slot_pos"], T, K, dtype), dtype)
+    b = oracle.combine_by_perm(y, r["packed_weights"], r["perm"], T, dtype)
+    np.testing.assert_allclose(a, b, rtol=1e-2 if dtype else 1e-3, atol=1e-2 if dtype else 2e-3)
+
+
+def test_swiglu_expert_vs_torch_fp32():
+    import torch
+    rng = np.random.default_rng(4)
+    M, D, I = 5, 64, 48
+    x = oracle.f32_to_16(rng.standard_normal((M, D)).astype(np.float32), 1)
+    wgu = oracle.f32_to_16((rng.standard_normal((2 * I, D)) * 0.1).astype(np.float32), 1)
+    wdn = oracle.f32_to_16((rng.standard_normal((D, I)) * 0.1).astype(np.float32), 1)
+    h, y = oracle.swiglu_expert(x, wgu, wdn, 1)
+    xt = torch.from_numpy(oracle.to_f32(x, 1))
+    g = xt @ torch.from_numpy(oracle.to_f32(wgu[:I], 1)).T
+    u = xt @ torch.from_numpy(oracle.to_f32(wgu[I:], 1)).T
+    ht = (torch.nn.functional.silu(g) * u).to(torch.bfloat16).float()
+    yt = ht @ torch.from_numpy(oracle.to_f32(wdn, 1)).T
+    np.testing.assert_allclose(oracle.to_f32(h, 1), ht.numpy(), rtol=2e-2, atol=2e-2)
+    np.testing.assert_allclose(oracle.to_f32(y, 1), yt.numpy(), rtol=2e-2, atol=2e-2)

@@ -1,0 +1,224 @@
+"""GPU parity of the packing kernels (through the C ABI) against the oracle and
+the reference's golden vectors: bit-exact for every output."""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import moe_b200 as mb
+import oracle
+import routing
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+
+def to_dev_rows(u16, dtype=torch.float16):
+    return torch.from_numpy(np.ascontiguousarray(u16).view(np.int16)).view(dtype).cuda()
+
+
+def bits(t):
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def gpu_pack(emb_u16, asgn, wts, E, dtype=torch.float16, ws=None, repeat=1):
+    T = asgn.shape[0]
+    K = asgn.shape[1]
+    emb = to_dev_rows(emb_u16, dtype)
+    a = torch.from_numpy(np.ascontiguousarray(asgn, np.int32)).cuda()
+    w = torch.from_numpy(np.ascontiguousarray(wts, np.float32)).cuda() if wts is not None else None
+    ws = ws or mb.Workspace(T, K, E)
+    outs = []
+    for _ in range(repeat):
+        r = mb.pack(emb, a, w, E, workspace=ws)
+        torch.cuda.synchronize()
+        assert ws.device_status() == 0
+        outs.append(dict(packed=bits(r.packed),
+                         packed_weights=None if r.packed_weights is None else r.packed_weights.cpu().numpy(),
+                         perm=r.perm.cpu().numpy(), expert_count=r.expert_count.cpu().numpy(),
+                         expert_start=r.expert_start.cpu().numpy(), slot_pos=r.slot_pos.cpu().numpy()))
+    return outs
+
+
+def assert_same(g, o, E):
+    assert g["packed"].tobytes() == o["packed"].tobytes()
+    np.testing.assert_array_equal(g["perm"], o["perm"])
+    np.testing.assert_array_equal(g["expert_count"], o["expert_count"])
+    np.testing.assert_array_equal(g["expert_start"], o["expert_start"][:E + 1])
+    np.testing.assert_array_equal(g["slot_pos"], o["slot_pos"])
+    if o.get("packed_weights") is not None:
+        assert g["packed_weights"].tobytes() == o["packed_weights"].tobytes()
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLDEN, "*.npz"))), ids=os.path.basename)
+def test_pack_matches_reference_golden(cuda, path):
+    g = np.load(path)
+    E = int(g["E"])
+    asgn, wts = g["asgn"], g["wts"]
+    T = asgn.shape[0]
+    if "emb" in g:
+        emb = g["emb"]
+    else:  # the golden stores index outputs only: use seeded rows (packing is bitwise)
+        emb = np.random.default_rng(T).integers(0, 65536, (T, 64), dtype=np.uint16)
+    r = gpu_pack(emb, asgn, wts, E, repeat=2)
+    for x in r:
+        np.testing.assert_array_equal(x["perm"], g["perm"])
+        np.testing.assert_array_equal(x["expert_start"][:E], g["expert_start"])
+        assert x["expert_start"][E] == asgn.size
+        np.testing.assert_array_equal(x["expert_count"], g["expert_count"])
+        assert x["packed_weights"].tobytes() == g["packed_weights"].tobytes()
+        if "packed" in g:
+            assert x["packed"].tobytes() == g["packed"].tobytes()
+        else:
+            assert x["packed"].tobytes() == emb[g["perm"]].tobytes()
+
+
+CASES = [
+    # T, K, E, d, dist
+    (1, 1, 1, 8, "uniform"),
+    (16, 2, 4, 8, "uniform"),
+    (512, 4, 60, 2048, "uniform"),      # C1
+    (1000, 3, 7, 24, "uniform"),        # vector path with a ragged row tail
+    (257, 2, 5, 20, "uniform"),         # d % 8 != 0: 2-byte path
+    (2049, 4, 60, 256, "zipf"),         # T*K not a multiple of the tile
+    (5000, 8, 128, 64, "uniform"),
+    (3000, 4, 1024, 16, "uniform"),     # E at the limit
+    (4096, 1, 64, 128, "zipf"),         # K = 1
+    (700, 32, 40, 16, "uniform"),       # K at the limit
+]
+
+
+@pytest.mark.parametrize("T,K,E,d,dist", CASES)
+def test_pack_matches_oracle(cuda, T, K, E, d, dist):
+    asgn, wts = routing.gen_routing(T, K, E, dist, seed=T + K)
+    emb = np.random.default_rng(d).integers(0, 65536, (T, d), dtype=np.uint16)
+    o = oracle.scatter(emb, asgn, wts, E)
+    for g in gpu_pack(emb, asgn, wts, E, repeat=2):
+        assert_same(g, o, E)
+
+
+def test_pack_bf16_rows_and_empty_experts(cuda):
+    T, K, E, d = 3000, 4, 100, 64
+    rng = np.random.default_rng(5)
+    asgn = np.stack([rng.choice(np.arange(10, 30), K, replace=False) for _ in range(T)]).astype(np.int32)
+    wts = rng.random((T, K)).astype(np.float32)
+    emb = rng.integers(0, 65536, (T, d), dtype=np.uint16)
+    o = oracle.scatter(emb, asgn, wts, E)
+    g = gpu_pack(emb, asgn, wts, E, dtype=torch.bfloat16)[0]
+    assert_same(g, o, E)
+    assert (g["expert_count"][:10] == 0).all() and (g["expert_count"][30:] == 0).all()
+
+
+def test_pack_without_weights(cuda):
+    T, K, E, d = 600, 2, 9, 32
+    asgn, _ = routing.gen_routing(T, K, E, "uniform", seed=9)
+    emb = np.random.default_rng(9).integers(0, 65536, (T, d), dtype=np.uint16)
+    o = oracle.scatter(emb, asgn, None, E)
+    g = gpu_pack(emb, asgn, None, E)[0]
+    assert_same(g, o, E)
+
+
+def test_pack_empty(cuda):
+    E = 5
+    ws = mb.Workspace(0, 2, E)
+    emb = torch.empty((0, 8), dtype=torch.float16, device="cuda")
+    a = torch.empty((0, 2), dtype=torch.int32, device="cuda")
+    r = mb.pack(emb, a, None, E, workspace=ws)
+    torch.cuda.synchronize()
+    assert r.expert_count.cpu().tolist() == [0] * E
+    assert r.expert_start.cpu().tolist() == [0] * (E + 1)
+
+
+def test_pack_reports_bad_assignment(cuda):
+    T, K, E, d = 100, 2, 6, 16
+    asgn, wts = routing.gen_routing(T, K, E, "uniform", seed=1)
+    asgn[37, 1] = E       # outside [0, E)
+    asgn[50, 0] = -3
+    emb = torch.zeros((T, d), dtype=torch.float16, device="cuda")
+    ws = mb.Workspace(T, K, E)
+    mb.pack(emb, torch.from_numpy(asgn).cuda(), torch.from_numpy(wts).cuda(), E, workspace=ws)
+    st = ws.device_status()
+    assert st & mb.DEV_BAD_ASSIGNMENT
+    assert not st & mb.DEV_WAIT_TIMEOUT
+    # the workspace stays usable: a clean call after the bad one is exact
+    asgn2, wts2 = routing.gen_routing(T, K, E, "uniform", seed=2)
+    embn = np.random.default_rng(3).integers(0, 65536, (T, d), dtype=np.uint16)
+    g = gpu_pack(embn, asgn2, wts2, E, ws=ws)[0]
+    assert_same(g, oracle.scatter(embn, asgn2, wts2, E), E)
+
+
+def test_iscatter_python_boundary(cuda):
+    """make_scatter('b200').run(...) into MoEBuffers, as the reference harnesses call it."""
+    T, K, E, d = 2048, 4, 64, 256
+    asgn, wts = routing.gen_routing(T, K, E, "zipf", seed=4)
+    emb_u16 = np.random.default_rng(4).integers(0, 65536, (T, d), dtype=np.uint16)
+    p = mb.MoEParams(T=T, K=K, E=E, d_model=d)
+    s = mb.make_scatter("b200")
+    bufs = mb.allocate_buffers(p)
+    emb = to_dev_rows(emb_u16)
+    a = torch.from_numpy(asgn).cuda()
+    w = torch.from_numpy(wts).cuda()
+    o = oracle.scatter(emb_u16, asgn, wts, E)
+    for _ in range(3):  # back to back, no re-zeroing by the caller
+        t = s.run(emb, a, w, bufs, p)
+        torch.cuda.synchronize()
+        assert t.total_ms == 0.0
+        assert bits(bufs.packed).tobytes() == o["packed"].tobytes()
+        np.testing.assert_array_equal(bufs.perm.cpu().numpy(), o["perm"])
+        np.testing.assert_array_equal(bufs.expert_start.cpu().numpy(), o["expert_start"])
+
+
+def _check_stable_pack_on_device(emb, asgn, wts, r, E):
+    """Size-independent characterisation of the stable pack, all on the GPU:
+    key(pos) = expert * T*K + slot strictly increases with pos, packed = emb[perm],
+    perm = slot // K, packed_weights = wts[slot], counts = bincount, starts = cumsum."""
+    T, K = asgn.shape
+    TK = T * K
+    sp = r.slot_pos.long()
+    slot_of_pos = torch.empty(TK, dtype=torch.long, device="cuda")
+    slot_of_pos[sp] = torch.arange(TK, device="cuda")
+    af = asgn.reshape(-1).long()
+    key = af[slot_of_pos] * TK + slot_of_pos
+    assert bool((key[1:] > key[:-1]).all())
+    assert torch.equal(r.perm.long(), slot_of_pos // K)
+    assert torch.equal(r.packed_weights, wts.reshape(-1)[slot_of_pos])
+    cnt = torch.bincount(af, minlength=E).int()
+    assert torch.equal(r.expert_count, cnt)
+    start = torch.zeros(E + 1, dtype=torch.int64, device="cuda")
+    start[1:] = torch.cumsum(cnt.long(), 0)
+    assert torch.equal(r.expert_start.long(), start)
+    step = 1 << 16
+    ev = emb.view(torch.int16)
+    pv = r.packed.view(torch.int16)
+    for i in range(0, TK, step):
+        assert torch.equal(pv[i:i + step], ev[r.perm[i:i + step].long()])
+
+
+def test_pack_c2_full_size_vs_oracle(cuda):
+    c = routing.CONFIGS["c2"]
+    asgn, wts = routing.gen_routing(c["T"], c["K"], c["E"], c["dist"], c["seed"])
+    emb = routing.gen_rows(c["T"], c["d"], c["dtype"], c["seed"], device="cuda")
+    e16 = bits(emb)
+    o = oracle.scatter(e16, asgn, wts, c["E"])
+    g = gpu_pack(e16, asgn, wts, c["E"], repeat=2)
+    for x in g:
+        assert_same(x, o, c["E"])
+
+
+def test_pack_c3_full_size_properties(cuda):
+    c = routing.CONFIGS["c3"]
+    asgn_np, wts_np = routing.gen_routing(c["T"], c["K"], c["E"], c["dist"], c["seed"])
+    emb = routing.gen_rows(c["T"], c["d"], c["dtype"], c["seed"], device="cuda")
+    asgn = torch.from_numpy(asgn_np).cuda()
+    wts = torch.from_numpy(wts_np).cuda()
+    ws = mb.Workspace(c["T"], c["K"], c["E"])
+    r1 = mb.pack(emb, asgn, wts, c["E"], workspace=ws)
+    assert ws.device_status() == 0
+    _check_stable_pack_on_device(emb, asgn, wts, r1, c["E"])
+    # deterministic: a second call reproduces every output bit for bit
+    perm1 = r1.perm.clone()
+    r2 = mb.pack(emb, asgn, wts, c["E"], workspace=ws, out=r1)
+    assert ws.device_status() == 0
+    assert torch.equal(r2.perm, perm1)

@@ -1,0 +1,83 @@
+"""GPU parity of the weighted unpermute / combine against the oracle.
+
+Tolerance stated by the path's contract: 1e-3 relative (fp16 output) of the
+fp32-accumulated reference sum.  The kernel sums in the same order with the
+same fused multiply-adds as the oracle, so the test also holds it to bit
+equality with the oracle, which is the stronger check."""
+import numpy as np
+import pytest
+import torch
+
+import moe_b200 as mb
+import oracle
+import routing
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-3
+
+
+def to_dev(u16, dtype):
+    return torch.from_numpy(np.ascontiguousarray(u16).view(np.int16)).view(dtype).cuda()
+
+
+def bits(t):
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def within_tol(got_u16, want_u16, dt, rtol):
+    g = oracle.to_f32(got_u16, dt)
+    w = oracle.to_f32(want_u16, dt)
+    # half-ulp of the output format on top of the relative bound
+    ulp = 2.0 ** -10 if dt == 0 else 2.0 ** -7
+    return np.all(np.abs(g - w) <= rtol * np.abs(w) + ulp * np.abs(w) + 1e-6)
+
+
+@pytest.mark.parametrize("T,K,E,d", [(1, 1, 1, 8), (16, 2, 4, 8), (512, 4, 60, 2048),
+                                     (1000, 3, 7, 24), (257, 2, 5, 20), (3000, 8, 128, 64),
+                                     (700, 32, 40, 16)])
+@pytest.mark.parametrize("dt", [0, 1])
+def test_unpermute_matches_oracle(cuda, T, K, E, d, dt):
+    tdt = torch.float16 if dt == 0 else torch.bfloat16
+    asgn, wts = routing.gen_routing(T, K, E, "zipf", seed=T)
+    rng = np.random.default_rng(T + d)
+    emb = oracle.f32_to_16(rng.standard_normal((T, d)).astype(np.float32), dt)
+    o = oracle.scatter(emb, asgn, wts, E)
+    y = oracle.f32_to_16(rng.standard_normal((T * K, d)).astype(np.float32), dt)  # expert outputs
+    want = oracle.combine(y, o["packed_weights"], o["slot_pos"], T, K, dt)
+    got = mb.unpermute(to_dev(y, tdt), torch.from_numpy(o["packed_weights"]).cuda(),
+                       torch.from_numpy(o["slot_pos"]).cuda(), T, K)
+    g = bits(got)
+    assert within_tol(g, want, dt, RTOL)
+    assert g.tobytes() == want.tobytes()
+
+
+def test_pack_then_unpermute_identity_expert_c2(cuda):
+    """Identity expert at the full C2 size: out[t] = round16(sum_k w[t,k] * emb[t])."""
+    c = routing.CONFIGS["c2"]
+    T, K, E, d = c["T"], c["K"], c["E"], c["d"]
+    asgn, wts = routing.gen_routing(T, K, E, c["dist"], c["seed"])
+    emb = routing.gen_rows(T, d, c["dtype"], c["seed"], device="cuda")
+    a = torch.from_numpy(asgn).cuda()
+    w = torch.from_numpy(wts).cuda()
+    r = mb.pack(emb, a, w, E)
+    out = mb.unpermute(r.packed, r.packed_weights, r.slot_pos, T, K)
+    ref = (w.sum(dim=1, keepdim=True) * emb.float())
+    torch.testing.assert_close(out.float(), ref, rtol=RTOL, atol=1e-3)
+    want = oracle.combine(bits(r.packed), r.packed_weights.cpu().numpy(), r.slot_pos.cpu().numpy(), T, K, 0)
+    assert bits(out).tobytes() == want.tobytes()
+
+
+def test_unpermute_agrees_with_reference_formulation(cuda):
+    """The reference sums via fp32 atomics in packed order (bench_e2e.cu:136-152);
+    same values within tolerance."""
+    T, K, E, d = 2048, 4, 64, 128
+    asgn, wts = routing.gen_routing(T, K, E, "zipf", seed=7)
+    rng = np.random.default_rng(7)
+    emb = oracle.f32_to_16(rng.standard_normal((T, d)).astype(np.float32), 0)
+    o = oracle.scatter(emb, asgn, wts, E)
+    y = oracle.f32_to_16(rng.standard_normal((T * K, d)).astype(np.float32), 0)
+    ref32 = oracle.combine_by_perm(y, o["packed_weights"], o["perm"], T, 0)
+    got = mb.unpermute(to_dev(y, torch.float16), torch.from_numpy(o["packed_weights"]).cuda(),
+                       torch.from_numpy(o["slot_pos"]).cuda(), T, K)
+    np.testing.assert_allclose(got.float().cpu().numpy(), ref32, rtol=RTOL, atol=2e-3)
