@@ -98,6 +98,32 @@ int moe_b200_pack(const void* emb, const int32_t* asgn, const float* wts,
 int moe_b200_workspace_status(void* workspace, size_t workspace_bytes, void* stream,
                               int* device_status /* host */);
 
+/* Scratch bytes built into the library for moe_b200_pack_noalloc, per device. */
+#define MOE_B200_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* moe_b200_pack for callers that cannot allocate device memory.  This entry
+ * point has no counterpart in the reference.  Some callers own only their
+ * inputs and outputs: a plugin inside a host framework that hands out device
+ * memory from its own pool and forbids direct cudaMalloc, or a thin FFI
+ * binding with no allocator of its own.  Here the scratch is a 4 MiB array
+ * built into the library (every GPU that loads the library holds it until
+ * exit); the caller passes only inputs and outputs, with the same meaning as
+ * in moe_b200_pack.  Shapes whose scratch (moe_b200_pack_workspace_bytes)
+ * exceeds MOE_B200_NOALLOC_SCRATCH_BYTES are rejected with
+ * MOE_B200_ERR_WORKSPACE (e.g. T*K above ~1M slots).
+ *  - The first call on each device, made with that device current, looks up
+ *    the array's address and zero-fills it (blocking); make that first call
+ *    before any stream capture.
+ *  - All calls on a device share the array: calls that overlap on the GPU
+ *    race and must be serialised by the caller.
+ *  - Device-side conditions (MOE_B200_DEV_*) are not reported by this entry
+ *    point.  No cudaMalloc, cudaFree or allocating routine is called.       */
+int moe_b200_pack_noalloc(const void* emb, const int32_t* asgn, const float* wts,
+                          int T, int K, int E, int d,
+                          void* packed, float* packed_weights, int32_t* perm,
+                          int32_t* expert_count, int32_t* expert_start, int32_t* slot_pos,
+                          void* stream);
+
 /* ------------------------------------------------------------ combine ---- */
 
 /* Weighted unpermute + top-K combine:
