@@ -12,50 +12,36 @@ namespace moe_b200 {
 
 // ---------------------------------------------------------------- layout ----
 // Packing workspace (all offsets 256-byte aligned):
-//   [0, 256)          WsHeader: tile ticket, finished-tile counter, device
-//                     condition bits
+//   [0, 256)          WsHeader: tile ticket, device condition bits
 //   tile_status       num_tiles * E  u64 words of the decoupled look-back
 //   rank              T*K int32: rank of slot (t, k) among the earlier slots
 //                     routed to the same expert
-// The route/scan kernel leaves ticket, counter and tile_status at zero when it
-// finishes, so a workspace zero-filled once stays valid for every later call.
+// pack_rows re-zeroes the ticket and tile_status after the route/scan kernel
+// has finished, so a workspace zero-filled once stays valid for every later
+// call.
 struct WsHeader {
     uint32_t ticket;
-    uint32_t done;
     uint32_t status;
-    uint32_t pad[61];
+    uint32_t pad[62];
 };
 static_assert(sizeof(WsHeader) == 256, "header is one 256-byte block");
 
-constexpr int kScanThreads = 256;           // route/scan CTA size (8 warps)
-constexpr int kScanWarps = kScanThreads / 32;
-constexpr int kSlotsPerWarpChunk = 32;
-constexpr int kBaseTileSlots = kScanThreads * 8;  // 2048 slots per tile
-constexpr size_t kMaxStatusBytes = size_t(16) << 20;
+constexpr int kScanWarps = 8;                    // route/scan CTA: 8 warps
+constexpr int kScanThreads = kScanWarps * 32;
+constexpr int kScanChunks = 8;                   // 32-slot chunks per warp
+constexpr int kTileSlots = kScanThreads * kScanChunks;  // 2048 slots per tile
 
 struct PackPlan {
-    int tile_slots;   // slots per route/scan tile
     int num_tiles;
     size_t status_off, rank_off, total_bytes;
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// Tile size grows in powers of two only when the look-back status array would
-// exceed kMaxStatusBytes (very large T*K times E).
 inline PackPlan plan_pack(int T, int K, int E) {
     PackPlan p{};
     int64_t TK = int64_t(T) * K;
-    int64_t tile = kBaseTileSlots;
-    while (true) {
-        int64_t nt = (TK + tile - 1) / tile;
-        if (size_t(nt) * size_t(E) * 8 <= kMaxStatusBytes || tile >= (int64_t(1) << 24)) {
-            p.tile_slots = int(tile);
-            p.num_tiles = int(nt);
-            break;
-        }
-        tile *= 2;
-    }
+    p.num_tiles = int((TK + kTileSlots - 1) / kTileSlots);
     p.status_off = sizeof(WsHeader);
     p.rank_off = p.status_off + align256(size_t(p.num_tiles) * size_t(E) * 8);
     p.total_bytes = p.rank_off + align256(size_t(TK) * 4);
@@ -108,5 +94,109 @@ __device__ __forceinline__ void pdl_wait_primary() {
 // roughly 1 s); past it the kernel records MOE_B200_DEV_WAIT_TIMEOUT and
 // moves on instead of spinning forever.
 constexpr uint32_t kMaxPolls = 1u << 24;
+
+// ------------------------------------------------ mbarrier / bulk copies ----
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete: gives up
+// after kWaitLimitNs of wall time and returns false.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
+// Bulk (non-tensor) copy global -> shared, completing on an mbarrier.  Both
+// addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                         uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Bulk copy shared -> global, tracked by the issuing thread's bulk group.
+__device__ __forceinline__ void bulk_s2g(void* gmem_dst, const void* smem_src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gmem_dst),
+                 "r"(smem_u32(smem_src)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed bulk groups of this thread still READ shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+uint32_t* device_status_word();  // status.cu
+
+// Launch configuration that lets the kernel start while the previous kernel
+// in the stream finishes (programmatic dependent launch); the kernel must call
+// pdl_wait_primary() before touching anything the previous kernel writes.
+inline cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    return cfg;
+}
+inline cudaLaunchAttribute pdl_attr() {
+    cudaLaunchAttribute a;
+    a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    a.val.programmaticStreamSerializationAllowed = 1;
+    return a;
+}
 
 }  // namespace moe_b200

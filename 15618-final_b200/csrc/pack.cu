@@ -7,26 +7,29 @@
 // Two kernels, one stream, no CUB and no host round trip:
 //
 //  1. route_scan_kernel  (reads T*K*4 bytes of assignments)
-//     One CTA per tile of slots, tiles claimed in order through an atomic
-//     ticket so that every earlier tile is already running (forward progress
-//     of the look-back).  Per tile: a warp-level __match_any_sync histogram
-//     (pass 1), a per-expert prefix over the tile's warps, then a decoupled
-//     look-back across tiles, one thread per expert, that turns the tile's
-//     per-expert counts into its exclusive prefix.  Pass 2 replays the
-//     match-any ranking to give every slot its rank among earlier slots of
-//     the same expert.  The last CTA to finish turns the final inclusive
-//     prefix into expert_count / expert_start and re-zeroes the scratch.
+//     One CTA per tile of 2048 slots, tiles claimed in order through an
+//     atomic ticket so that every earlier tile is already running (forward
+//     progress of the look-back).  Per tile: each lane loads its 8 slots at
+//     once; a warp-level __match_any_sync pass ranks every slot among the
+//     earlier slots of the same expert in the warp and builds per-warp
+//     histograms; a per-expert prefix over the warps and a decoupled look-back
+//     across tiles (one thread per expert) turn that into a global rank.  The
+//     last tile holds the final inclusive prefix and writes expert_count /
+//     expert_start.
 //
 //  2. pack_rows_kernel  (the HBM-bound copy)
 //     One warp per token: the token row is read ONCE into registers with
 //     16-byte loads and stored to its K packed rows, pos = expert_start[e] +
 //     rank.  It is launched as a programmatic dependent of kernel 1: its CTAs
 //     start loading rows while kernel 1 is still scanning and only wait for
-//     kernel 1 before reading rank / expert_start.
+//     kernel 1 before reading rank / expert_start; afterwards they re-zero the
+//     look-back scratch for the next call.
 //
 // The reference strategies replaced here re-read each token row once per slot
 // (src/scatter/scatter_csort.cu:57-91, scatter_vec.cu:79-103) and pay a CUB
 // sort or scan plus host-synchronising timers between launches.
+#include <cstdlib>
+
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -35,6 +38,8 @@ namespace moe_b200 {
 
 constexpr uint64_t kFlagAggregate = uint64_t(1) << 32;
 constexpr uint64_t kFlagInclusive = uint64_t(2) << 32;
+// Shared-memory row ring of the bulk packer (per CTA; two CTAs per SM).
+constexpr size_t kPackRingBytes = 100 * 1024;
 
 __device__ __forceinline__ void record_status(WsHeader* hdr, uint32_t bits) {
     atomicOr(&hdr->status, bits);
@@ -56,137 +61,125 @@ __device__ __forceinline__ uint64_t wait_status(const uint64_t* word, WsHeader* 
     return s;
 }
 
-// Loads the expert of slot idx for this lane; -1 for padding past T*K or for
-// an out-of-range assignment (which is also recorded).
-__device__ __forceinline__ int load_expert(const int32_t* __restrict__ asgn, int64_t idx,
-                                           int64_t TK, int E, WsHeader* hdr) {
-    if (idx >= TK) return -1;
-    int e = __ldg(asgn + idx);
-    if (e < 0 || e >= E) {
-        record_status(hdr, MOE_B200_DEV_BAD_ASSIGNMENT);
-        return -1;
-    }
-    return e;
+// Raw assignment of slot idx (-1 past the end).
+__device__ __forceinline__ int load_slot(const int32_t* __restrict__ asgn, int64_t idx, int64_t TK) {
+    return idx < TK ? __ldg(asgn + idx) : -1;
 }
 
 __global__ void __launch_bounds__(kScanThreads)
-route_scan_kernel(const int32_t* __restrict__ asgn, int64_t TK, int E, int tile_slots,
-                  int num_tiles, WsHeader* __restrict__ hdr, uint64_t* __restrict__ status,
+route_scan_kernel(const int32_t* __restrict__ asgn, int64_t TK, int E, int num_tiles,
+                  WsHeader* __restrict__ hdr, uint64_t* __restrict__ status,
                   int32_t* __restrict__ rank, int32_t* __restrict__ expert_count,
                   int32_t* __restrict__ expert_start) {
     // Let the row-copy kernel get resident while this one scans.
     pdl_launch_dependents();
 
     extern __shared__ int32_t smem[];
-    int32_t* hist = smem;                   // [kScanWarps][E]
+    int32_t* hist = smem;                        // [kScanWarps][E]
     int32_t* tile_excl = smem + kScanWarps * E;  // [E] exclusive prefix of this tile
-    int32_t* tile_agg = tile_excl + E;      // [E] this tile's counts
+    int32_t* tile_agg = tile_excl + E;           // [E] this tile's counts
     __shared__ int s_tile;
-    __shared__ int s_last;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t lt = lanemask_lt();
+
+    // Tiles are claimed through a ticket so that every earlier tile is already
+    // running when this one looks back.  The slots of the likely tile
+    // (blockIdx.x) are loaded while the ticket round-trip is in flight.
+    int tile = blockIdx.x;
+    int e[kScanChunks];
+    {
+        const int64_t base = int64_t(tile) * kTileSlots + warp * (kScanChunks * 32) + lane;
+#pragma unroll
+        for (int c = 0; c < kScanChunks; ++c) e[c] = load_slot(asgn, base + c * 32, TK);
+    }
     if (tid == 0) s_tile = int(atomicAdd(&hdr->ticket, 1u));
     for (int i = tid; i < kScanWarps * E; i += kScanThreads) hist[i] = 0;
     __syncthreads();
-    const int tile = s_tile;
+    if (s_tile != tile) {  // CTA-uniform; rare
+        tile = s_tile;
+        const int64_t base = int64_t(tile) * kTileSlots + warp * (kScanChunks * 32) + lane;
+#pragma unroll
+        for (int c = 0; c < kScanChunks; ++c) e[c] = load_slot(asgn, base + c * 32, TK);
+    }
+    const int64_t warp_base = int64_t(tile) * kTileSlots + warp * (kScanChunks * 32);
 
-    // Each warp owns a contiguous run of the tile's slots.
-    const int warp_slots = tile_slots / kScanWarps;
-    const int64_t warp_base = int64_t(tile) * tile_slots + int64_t(warp) * warp_slots;
+    // Per-warp ranking via match-any groups, in slot order: r = earlier slots
+    // of the same expert within this warp's run; one smem update per group.
     int32_t* my_hist = hist + warp * E;
-    const uint32_t lt = lanemask_lt();
-
-    // Pass 1: per-warp histogram via match-any groups (one smem update per
-    // distinct expert per 32 slots).
-    for (int c = 0; c < warp_slots; c += kSlotsPerWarpChunk) {
-        int e = load_expert(asgn, warp_base + c + lane, TK, E, hdr);
-        uint32_t peers = __match_any_sync(0xffffffffu, e);
-        if (e >= 0 && (peers & lt) == 0) my_hist[e] += __popc(peers);
+    int r[kScanChunks];
+#pragma unroll
+    for (int c = 0; c < kScanChunks; ++c) {
+        int ec = e[c];
+        if (ec >= E || (ec < 0 && warp_base + c * 32 + lane < TK)) {
+            record_status(hdr, MOE_B200_DEV_BAD_ASSIGNMENT);
+            ec = -1;
+        }
+        e[c] = ec;
+        const uint32_t peers = __match_any_sync(0xffffffffu, ec);
+        const int32_t b = ec >= 0 ? my_hist[ec] : 0;
         __syncwarp();
+        if (ec >= 0 && (peers & lt) == 0) my_hist[ec] = b + __popc(peers);
+        __syncwarp();
+        r[c] = b + __popc(peers & lt);
     }
     __syncthreads();
 
     // Per expert: exclusive prefix over the tile's warps; publish the tile
     // aggregate (tile 0 publishes its inclusive prefix directly).
-    for (int e = tid; e < E; e += kScanThreads) {
+    for (int x = tid; x < E; x += kScanThreads) {
         int32_t run = 0;
+#pragma unroll
         for (int w = 0; w < kScanWarps; ++w) {
-            int32_t v = hist[w * E + e];
-            hist[w * E + e] = run;
+            int32_t v = hist[w * E + x];
+            hist[w * E + x] = run;
             run += v;
         }
-        tile_agg[e] = run;
-        uint64_t flag = tile == 0 ? kFlagInclusive : kFlagAggregate;
-        st_relaxed_u64(status + size_t(tile) * E + e, flag | uint32_t(run));
+        tile_agg[x] = run;
+        st_relaxed_u64(status + size_t(tile) * E + x,
+                       (tile == 0 ? kFlagInclusive : kFlagAggregate) | uint32_t(run));
     }
 
-    // Decoupled look-back, one thread per expert: walk predecessor tiles
-    // (loads issued 8 at a time), summing aggregates until an inclusive prefix.
-    for (int e = tid; e < E; e += kScanThreads) {
+    // Decoupled look-back, one thread per expert: predecessor words are loaded
+    // 8 at a time; aggregates are summed until an inclusive prefix is found.
+    for (int x = tid; x < E; x += kScanThreads) {
         int32_t excl = 0;
-        if (tile > 0) {
-            int j = tile - 1;
-            bool found = false;
-            while (!found && j >= 0) {
-                uint64_t s[8];
+        int j = tile - 1;
+        bool found = tile == 0;
+        while (!found) {
+            uint64_t w8[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    s[i] = (j - i >= 0) ? ld_relaxed_u64(status + size_t(j - i) * E + e)
-                                        : kFlagInclusive;
+            for (int i = 0; i < 8; ++i)
+                w8[i] = (j - i >= 0) ? ld_relaxed_u64(status + size_t(j - i) * E + x) : kFlagInclusive;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    if (found) break;
-                    if (j - i < 0) { found = true; break; }
-                    uint64_t w = s[i];
-                    if ((w >> 32) == 0) w = wait_status(status + size_t(j - i) * E + e, hdr);
+            for (int i = 0; i < 8; ++i) {
+                if (!found) {
+                    uint64_t w = w8[i];
+                    if (j - i >= 0 && (w >> 32) == 0) w = wait_status(status + size_t(j - i) * E + x, hdr);
                     excl += int32_t(uint32_t(w));
                     if ((w >> 32) == 2) found = true;
                 }
-                j -= 8;
             }
+            j -= 8;
         }
-        tile_excl[e] = excl;
-        st_relaxed_u64(status + size_t(tile) * E + e,
-                       kFlagInclusive | uint32_t(excl + tile_agg[e]));
-        // Seed every warp's running rank with the tile prefix.
-        for (int w = 0; w < kScanWarps; ++w) hist[w * E + e] += excl;
+        tile_excl[x] = excl;
+        if (tile > 0)
+            st_relaxed_u64(status + size_t(tile) * E + x, kFlagInclusive | uint32_t(excl + tile_agg[x]));
     }
     __syncthreads();
 
-    // Pass 2: replay the match-any ranking; rank = running count of the
-    // expert before this slot (global across tiles).
-    for (int c = 0; c < warp_slots; c += kSlotsPerWarpChunk) {
-        int64_t idx = warp_base + c + lane;
-        int e = (idx < TK) ? __ldg(asgn + idx) : -1;
-        if (e >= E) e = -1;
-        uint32_t peers = __match_any_sync(0xffffffffu, e);
-        int32_t base = e >= 0 ? my_hist[e] : 0;
-        __syncwarp();
-        if (e >= 0 && (peers & lt) == 0) my_hist[e] = base + __popc(peers);
-        __syncwarp();
-        if (idx < TK) rank[idx] = e >= 0 ? base + __popc(peers & lt) : -1;
+#pragma unroll
+    for (int c = 0; c < kScanChunks; ++c) {
+        const int64_t idx = warp_base + c * 32 + lane;
+        if (idx < TK) rank[idx] = e[c] >= 0 ? tile_excl[e[c]] + my_hist[e[c]] + r[c] : -1;
     }
 
-    // The last CTA to finish publishes counts / starts and re-zeroes scratch.
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(&hdr->done, 1u) == uint32_t(num_tiles - 1));
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-
-    // Block-wide exclusive scan over E of the final inclusive counts: each
-    // thread owns a contiguous run of experts.
+    // The last tile holds the final inclusive prefix: publish counts / starts.
+    if (tile != num_tiles - 1) return;
     const int per = (E + kScanThreads - 1) / kScanThreads;
     const int e0 = tid * per;
     int32_t local = 0;
-    for (int i = 0; i < per && e0 + i < E; ++i) {
-        uint64_t w = ld_relaxed_u64(status + size_t(num_tiles - 1) * E + e0 + i);
-        int32_t cnt = int32_t(uint32_t(w));
-        tile_agg[e0 + i] = cnt;
-        local += cnt;
-    }
-    // warp scan of thread totals, then across the 8 warps
+    for (int i = 0; i < per && e0 + i < E; ++i) local += tile_excl[e0 + i] + tile_agg[e0 + i];
     int32_t incl = local;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -200,20 +193,21 @@ route_scan_kernel(const int32_t* __restrict__ asgn, int64_t TK, int E, int tile_
     for (int w = 0; w < warp; ++w) warp_off += warp_tot[w];
     int32_t run = warp_off + incl - local;
     for (int i = 0; i < per && e0 + i < E; ++i) {
-        int32_t cnt = tile_agg[e0 + i];
+        const int32_t cnt = tile_excl[e0 + i] + tile_agg[e0 + i];
         expert_count[e0 + i] = cnt;
         expert_start[e0 + i] = run;
         run += cnt;
     }
     if (tid == kScanThreads - 1) expert_start[E] = warp_off + incl;
+}
 
-    // Leave the scratch zero-filled for the next call.
-    const size_t words = size_t(num_tiles) * E;
-    for (size_t i = tid; i < words; i += kScanThreads) status[i] = 0;
-    if (tid == 0) {
-        hdr->ticket = 0;
-        hdr->done = 0;
-    }
+// After the route/scan grid has finished (PDL wait done): re-zero its ticket
+// and look-back words so the workspace is ready for the next call.
+__device__ __forceinline__ void rearm_scan_scratch(WsHeader* hdr, uint64_t* status, size_t words) {
+    const size_t gt = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t nt = size_t(gridDim.x) * blockDim.x;
+    for (size_t i = gt; i < words; i += nt) status[i] = 0;
+    if (gt == 0) hdr->ticket = 0;
 }
 
 // One warp per token; VPL 16-byte vectors per lane per pass over the row.
@@ -223,7 +217,8 @@ pack_rows_kernel(const uint4* __restrict__ emb, const int32_t* __restrict__ asgn
                  const float* __restrict__ wts, const int32_t* __restrict__ rank,
                  const int32_t* __restrict__ expert_start, int T, int K, int nvec,
                  uint4* __restrict__ packed, float* __restrict__ packed_w,
-                 int32_t* __restrict__ perm, int32_t* __restrict__ slot_pos) {
+                 int32_t* __restrict__ perm, int32_t* __restrict__ slot_pos,
+                 WsHeader* __restrict__ hdr, uint64_t* __restrict__ status, size_t status_words) {
     const int lane = threadIdx.x & 31;
     const int warps_per_cta = blockDim.x >> 5;
     const int64_t gw = int64_t(blockIdx.x) * warps_per_cta + (threadIdx.x >> 5);
@@ -279,6 +274,125 @@ pack_rows_kernel(const uint4* __restrict__ emb, const int32_t* __restrict__ asgn
         }
     }
     if (!waited) pdl_wait_primary();
+    rearm_scan_scratch(hdr, status, status_words);
+}
+
+// Persistent TMA bulk-copy row packer: one warp per CTA, a ring of R row
+// slots in shared memory.  Each CTA owns a contiguous token range.  Before
+// its PDL wait it issues cp.async.bulk loads of its first R token rows (the
+// rows are kernel inputs, so this overlaps the route/scan kernel).  After the
+// wait it computes the K packed positions of a group of G = 32 / K tokens at
+// once (lane l -> slot l % K of token l / K; expert_start cached in shared
+// memory), stores every row with K cp.async.bulk shared->global copies, and
+// refills a slot with the row R tokens ahead once the stores of the row it
+// held (issued kLag tokens earlier) have finished reading it.
+constexpr int kBulkLag = 2;
+
+__global__ void __launch_bounds__(32)
+pack_rows_bulk_kernel(const uint16_t* __restrict__ emb, const int32_t* __restrict__ asgn,
+                      const float* __restrict__ wts, const int32_t* __restrict__ rank,
+                      const int32_t* __restrict__ expert_start, int T, int K, int E, int d,
+                      int ring, uint16_t* __restrict__ packed, float* __restrict__ packed_w,
+                      int32_t* __restrict__ perm, int32_t* __restrict__ slot_pos,
+                      WsHeader* __restrict__ hdr, uint64_t* __restrict__ status,
+                      size_t status_words) {
+    extern __shared__ __align__(128) unsigned char ring_smem[];
+    const uint32_t rowb = uint32_t(d) * 2;
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring_smem + size_t(ring) * rowb);
+    int32_t* s_start = reinterpret_cast<int32_t*>(full + ring);  // [E]
+    const int lane = threadIdx.x;
+
+    const int64_t per = (int64_t(T) + gridDim.x - 1) / gridDim.x;
+    const int64_t t0 = int64_t(blockIdx.x) * per;
+    const int64_t n = t0 < T ? (T - t0 < per ? T - t0 : per) : 0;
+
+    if (lane == 0) {
+        for (int r = 0; r < ring; ++r) mbar_init(full + r, 1);
+        mbar_fence_init();
+    }
+    __syncwarp();
+    // Prefetch the first rows: inputs only, so no need to wait for the scan.
+    const int64_t pre = n < ring ? n : ring;
+    if (lane == 0) {
+        for (int64_t i = 0; i < pre; ++i) {
+            mbar_arrive_expect_tx(full + i, rowb);
+            bulk_g2s(ring_smem + size_t(i) * rowb, emb + (t0 + i) * d, rowb, full + i);
+        }
+    }
+    const int G = 32 / K;
+    const int gk = lane % K, gi = lane / K;
+    const bool lane_used = gi < G;
+    // Group inputs that do not depend on the scan.
+    auto load_inputs = [&](int64_t g, int& e, float& w) {
+        const int64_t i = g * G + gi;
+        e = -1;
+        w = 0.f;
+        if (lane_used && i < n) {
+            const int64_t s = (t0 + i) * K + gk;
+            e = __ldg(asgn + s);
+            if (packed_w) w = __ldg(wts + s);
+        }
+    };
+    int e_cur, e_nxt;
+    float w_cur, w_nxt;
+    load_inputs(0, e_cur, w_cur);
+
+    pdl_wait_primary();
+    rearm_scan_scratch(hdr, status, status_words);
+    for (int x = lane; x < E; x += 32) s_start[x] = expert_start[x];
+    __syncwarp();
+
+    // Position of this lane's slot in group g (after the scan).
+    auto position = [&](int64_t g, int e) -> int32_t {
+        const int64_t i = g * G + gi;
+        if (!lane_used || i >= n) return -1;
+        const int64_t s = (t0 + i) * K + gk;
+        const int32_t r = rank[s];
+        const int32_t pos = (r >= 0 && e >= 0 && e < E) ? s_start[e] + r : -1;
+        if (slot_pos) slot_pos[s] = pos;
+        return pos;
+    };
+    int32_t p_cur = position(0, e_cur);
+
+    bool ok = true;
+    for (int64_t g = 0; ok && g * G < n; ++g) {
+        load_inputs(g + 1, e_nxt, w_nxt);
+        if (p_cur >= 0) {
+            perm[p_cur] = int32_t(t0 + g * G + gi);
+            if (packed_w) packed_w[p_cur] = w_cur;
+        }
+        for (int q = 0; q < G; ++q) {
+            const int64_t i = g * G + q;
+            if (i >= n) break;
+            const int slot = int(i % ring);
+            if (!mbar_wait(full + slot, uint32_t(i / ring) & 1u)) {
+                if (lane == 0) atomicOr(&hdr->status, MOE_B200_DEV_WAIT_TIMEOUT);
+                ok = false;
+                break;
+            }
+            if (lane_used && gi == q && p_cur >= 0)
+                bulk_s2g(packed + int64_t(p_cur) * d, ring_smem + size_t(slot) * rowb, rowb);
+            bulk_commit();
+            // Refill the slot of token i - kLag once its stores have read it.
+            const int64_t j = i - kBulkLag;
+            if (j >= 0 && j + ring < n) {
+                bulk_wait_read<kBulkLag>();
+                __syncwarp();
+                if (lane == 0) {
+                    const int js = int(j % ring);
+                    mbar_arrive_expect_tx(full + js, rowb);
+                    bulk_g2s(ring_smem + size_t(js) * rowb, emb + (t0 + j + ring) * d, rowb, full + js);
+                }
+            }
+        }
+        e_cur = e_nxt;
+        w_cur = w_nxt;
+        if (ok) p_cur = position(g + 1, e_cur);
+    }
+    // Rows whose refill was skipped above (the last kLag tokens) need no wait;
+    // every store must finish before the shared memory it reads goes away.
+    bulk_wait<0>();
+    pdl_launch_dependents();
 }
 
 // Fallback for rows that are not 16-byte multiples / not 16-byte aligned:
@@ -288,8 +402,11 @@ pack_rows_scalar_kernel(const uint16_t* __restrict__ emb, const int32_t* __restr
                         const float* __restrict__ wts, const int32_t* __restrict__ rank,
                         const int32_t* __restrict__ expert_start, int T, int K, int d,
                         uint16_t* __restrict__ packed, float* __restrict__ packed_w,
-                        int32_t* __restrict__ perm, int32_t* __restrict__ slot_pos) {
+                        int32_t* __restrict__ perm, int32_t* __restrict__ slot_pos,
+                        WsHeader* __restrict__ hdr, uint64_t* __restrict__ status,
+                        size_t status_words) {
     pdl_wait_primary();
+    rearm_scan_scratch(hdr, status, status_words);
     const int lane = threadIdx.x & 31;
     const int warps_per_cta = blockDim.x >> 5;
     const int64_t gw = int64_t(blockIdx.x) * warps_per_cta + (threadIdx.x >> 5);
@@ -333,11 +450,11 @@ cudaError_t launch_pack(const void* emb, const int32_t* asgn, const float* wts, 
     uint64_t* status = reinterpret_cast<uint64_t*>(base + plan.status_off);
     int32_t* rank = reinterpret_cast<int32_t*>(base + plan.rank_off);
     const int64_t TK = int64_t(T) * K;
+    const size_t words = size_t(plan.num_tiles) * size_t(E);
 
     size_t smem = size_t(kScanWarps + 2) * E * sizeof(int32_t);
     route_scan_kernel<<<plan.num_tiles, kScanThreads, smem, stream>>>(
-        asgn, TK, E, plan.tile_slots, plan.num_tiles, hdr, status, rank, expert_count,
-        expert_start);
+        asgn, TK, E, plan.num_tiles, hdr, status, rank, expert_count, expert_start);
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return err;
 
@@ -360,17 +477,45 @@ cudaError_t launch_pack(const void* emb, const int32_t* asgn, const float* wts, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (vec) {
+    const size_t rowb = size_t(d) * 2;
+    const int ring = int(kPackRingBytes / rowb) < 64 ? int(kPackRingBytes / rowb) : 64;
+    const char* sel = getenv("MOE_B200_PACK");
+    const bool want_bulk = !(sel && sel[0] == 'r');
+    if (vec && want_bulk && ring >= 4) {
+        const int smem = int(ring * rowb + ring * 8 + E * 4 + 128);
+        err = cudaFuncSetAttribute(pack_rows_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   smem);
+        if (err != cudaSuccess) return err;
+        int per_sm = 0;
+        err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pack_rows_bulk_kernel, 32, smem);
+        if (err != cudaSuccess) return err;
+        if (per_sm < 1) per_sm = 1;
+        int64_t g = int64_t(sm_count()) * per_sm;
+        // keep at least a few tokens per CTA so the ring is used
+        int64_t gmax = (int64_t(T) + 3) / 4;
+        if (g > gmax) g = gmax;
+        if (g < 1) g = 1;
+        cfg.gridDim = dim3(unsigned(g));
+        cfg.blockDim = dim3(32);
+        cfg.dynamicSmemBytes = size_t(smem);
+        err = cudaLaunchKernelEx(&cfg, pack_rows_bulk_kernel, static_cast<const uint16_t*>(emb), asgn,
+                                 wts, static_cast<const int32_t*>(rank),
+                                 static_cast<const int32_t*>(expert_start), T, K, E, d, ring,
+                                 static_cast<uint16_t*>(packed), packed_w, perm, slot_pos, hdr, status,
+                                 words);
+    } else if (vec) {
         err = cudaLaunchKernelEx(&cfg, pack_rows_kernel<8>, static_cast<const uint4*>(emb), asgn,
                                  wts, static_cast<const int32_t*>(rank),
                                  static_cast<const int32_t*>(expert_start), T, K, d / 8,
-                                 static_cast<uint4*>(packed), packed_w, perm, slot_pos);
+                                 static_cast<uint4*>(packed), packed_w, perm, slot_pos, hdr,
+                                 status, words);
     } else {
         err = cudaLaunchKernelEx(&cfg, pack_rows_scalar_kernel,
                                  static_cast<const uint16_t*>(emb), asgn, wts,
                                  static_cast<const int32_t*>(rank),
                                  static_cast<const int32_t*>(expert_start), T, K, d,
-                                 static_cast<uint16_t*>(packed), packed_w, perm, slot_pos);
+                                 static_cast<uint16_t*>(packed), packed_w, perm, slot_pos, hdr,
+                                 status, words);
     }
     return err;
 }

@@ -10,6 +10,8 @@
 // HBM traffic is the algorithmic minimum: T*K*d*2 bytes read + T*d*2 written.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cstdlib>
+
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -57,6 +59,7 @@ __global__ void __launch_bounds__(256)
 unpermute_kernel(const uint4* __restrict__ y, const float* __restrict__ packed_w,
                  const int32_t* __restrict__ slot_pos, int T, int K, int nvec,
                  uint4* __restrict__ out) {
+    pdl_wait_primary();
     const int lane = threadIdx.x & 31;
     const int warps_per_cta = blockDim.x >> 5;
     const int64_t gw = int64_t(blockIdx.x) * warps_per_cta + (threadIdx.x >> 5);
@@ -103,12 +106,128 @@ unpermute_kernel(const uint4* __restrict__ y, const float* __restrict__ packed_w
     }
 }
 
+// TMA bulk-copy pipeline: per CTA one producer warp and kConsumerWarps
+// consumer warps.  For each of the CTA's tokens the producer's lanes k < K
+// issue one cp.async.bulk of row y[p_k] (d*2 bytes) into a shared-memory
+// stage; the consumers wait on the stage's mbarrier, accumulate the K rows in
+// fp32 (ascending k, one FMA per term), round once and store the output row.
+// `stages` stages per CTA keep stages*K rows in flight with no register cost.
+constexpr int kConsumerWarps = 4;
+constexpr int kBulkThreads = (kConsumerWarps + 1) * 32;
+
+template <int DT>
+__global__ void __launch_bounds__(kBulkThreads)
+unpermute_bulk_kernel(const uint16_t* __restrict__ y, const float* __restrict__ packed_w,
+                      const int32_t* __restrict__ slot_pos, int T, int K, int d, int stages,
+                      uint4* __restrict__ out, uint32_t* __restrict__ dev_status) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const uint32_t rowb = uint32_t(d) * 2;
+    const size_t stage_bytes = size_t(K) * rowb;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(stages) * stage_bytes);
+    uint64_t* empty = full + stages;
+    float* sw = reinterpret_cast<float*>(empty + stages);  // [stages][K] weights
+    int32_t* sp = reinterpret_cast<int32_t*>(sw + stages * K);  // [stages][K] rows
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    pdl_wait_primary();
+    if (tid == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, kConsumerWarps);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // Producer.  The CTA's tokens are t_i = blockIdx.x + i * gridDim.x.
+        // Lane l covers slot k = l % K of token i = g * G + l / K of group g
+        // (G = 32 / K tokens per group), so one load round trip fetches the
+        // row indices and weights of G tokens; the next group's are in flight
+        // while this group's copies are issued.
+        const int G = 32 / K;
+        const int gk = lane % K, gi = lane / K;
+        const bool lane_used = gi < G;
+        const int64_t n_mine = (T - 1 - int64_t(blockIdx.x)) / gridDim.x + 1;  // tokens of this CTA
+        auto fetch = [&](int64_t g, int32_t& p, float& w) {
+            const int64_t i = g * G + gi;
+            p = -1;
+            w = 0.f;
+            if (lane_used && i < n_mine) {
+                const int64_t t = int64_t(blockIdx.x) + i * gridDim.x;
+                p = __ldg(slot_pos + t * K + gk);
+                if (p >= 0) w = __ldg(packed_w + p);
+            }
+        };
+        int32_t p_cur, p_nxt;
+        float w_cur, w_nxt;
+        fetch(0, p_cur, w_cur);
+        bool ok = true;
+        for (int64_t g = 0; ok && g * G < n_mine; ++g) {
+            fetch(g + 1, p_nxt, w_nxt);
+            for (int q = 0; q < G; ++q) {
+                const int64_t i = g * G + q;
+                if (i >= n_mine) break;
+                const int s = int(i % stages);
+                const uint32_t ph = uint32_t(i / stages) & 1u;
+                if (!mbar_wait(empty + s, ph ^ 1u)) {
+                    if (lane == 0) atomicOr(dev_status, MOE_B200_DEV_WAIT_TIMEOUT);
+                    ok = false;
+                    break;
+                }
+                const bool mine = lane_used && gi == q;
+                if (mine) {
+                    sw[s * K + gk] = w_cur;
+                    sp[s * K + gk] = p_cur;
+                }
+                const uint32_t valid = __ballot_sync(0xffffffffu, mine && p_cur >= 0);
+                __syncwarp();
+                if (lane == 0) mbar_arrive_expect_tx(full + s, uint32_t(__popc(valid)) * rowb);
+                __syncwarp();
+                if (mine && p_cur >= 0)
+                    bulk_g2s(smem + size_t(s) * stage_bytes + size_t(gk) * rowb,
+                             y + int64_t(p_cur) * d, rowb, full + s);
+            }
+            p_cur = p_nxt;
+            w_cur = w_nxt;
+        }
+    } else {
+        const int ctid = tid;  // 0 .. 32*kConsumerWarps-1
+        const int nvec = d >> 3;
+        int64_t t = blockIdx.x;
+        for (int i = 0; t < T; t += gridDim.x, ++i) {
+            const int s = i % stages;
+            const uint32_t ph = uint32_t(i / stages) & 1u;
+            if (!mbar_wait(full + s, ph)) {
+                if (ctid == 0) atomicOr(dev_status, MOE_B200_DEV_WAIT_TIMEOUT);
+                break;
+            }
+            const unsigned char* st = smem + size_t(s) * stage_bytes;
+            uint4* dst = out + t * nvec;
+            for (int v = ctid; v < nvec; v += 32 * kConsumerWarps) {
+                float acc[8];
+#pragma unroll
+                for (int h = 0; h < 8; ++h) acc[h] = 0.f;
+                for (int k = 0; k < K; ++k) {
+                    if (sp[s * K + k] < 0) continue;
+                    const uint4 x = *reinterpret_cast<const uint4*>(st + size_t(k) * rowb + size_t(v) * 16);
+                    acc_vec<DT>(acc, sw[s * K + k], x);
+                }
+                st_v4(dst + v, pack_vec<DT>(acc));
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty + s);
+        }
+    }
+}
+
 // Fallback for rows that are not 16-byte multiples / not 16-byte aligned.
 template <int DT>
 __global__ void __launch_bounds__(256)
 unpermute_scalar_kernel(const uint16_t* __restrict__ y, const float* __restrict__ packed_w,
                         const int32_t* __restrict__ slot_pos, int T, int K, int d,
                         uint16_t* __restrict__ out) {
+    pdl_wait_primary();
     const int64_t n = int64_t(T) * d;
     for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += int64_t(gridDim.x) * blockDim.x) {
@@ -140,39 +259,71 @@ static int sm_count_unperm() {
     return n > 0 ? n : 148;
 }
 
+static int bulk_smem_bytes(int K, int d, int stages) {
+    return stages * (K * d * 2 + 2 * 8 + K * 8) + 128;
+}
+
 cudaError_t launch_unpermute(const void* y, const float* packed_w, const int32_t* slot_pos,
                              int T, int K, int d, int dtype, void* out, cudaStream_t stream) {
     const bool vec = (d % 8 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0) &&
                      (reinterpret_cast<uintptr_t>(out) % 16 == 0);
     const int threads = 256;
+    const int sms = sm_count_unperm();
+    // Bulk-copy pipeline when at least 2 stages of K rows fit in shared memory.
+    const size_t stage = size_t(K) * d * 2;
+    int stages = stage > 0 ? int((200 * 1024) / stage) : 0;
+    if (stages > 4) stages = 4;
+    const char* sel = getenv("MOE_B200_UNPERMUTE");
+    const bool want_bulk = !(sel && sel[0] == 'r');
+    if (vec && want_bulk && stages >= 2) {
+        uint32_t* st = device_status_word();
+        if (!st) return cudaErrorInvalidDevice;
+        const int smem = bulk_smem_bytes(K, d, stages);
+        auto kern = dtype == MOE_B200_F16 ? unpermute_bulk_kernel<MOE_B200_F16>
+                                          : unpermute_bulk_kernel<MOE_B200_BF16>;
+        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (err != cudaSuccess) return err;
+        int per_sm = 0;
+        err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kBulkThreads, smem);
+        if (err != cudaSuccess) return err;
+        if (per_sm < 1) per_sm = 1;
+        int64_t grid = int64_t(sms) * per_sm;
+        if (grid > T) grid = T;
+        cudaLaunchConfig_t cfg = pdl_config(dim3(unsigned(grid)), dim3(kBulkThreads), smem, stream);
+        cudaLaunchAttribute attr = pdl_attr();
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, kern, static_cast<const uint16_t*>(y), packed_w, slot_pos, T, K,
+                                  d, stages, static_cast<uint4*>(out), st);
+    }
     if (vec) {
         const int warps_per_cta = threads / 32;
         int64_t want = (int64_t(T) + warps_per_cta - 1) / warps_per_cta;
-        int64_t cap = int64_t(sm_count_unperm()) * 64;
+        int64_t cap = int64_t(sms) * 64;
         int grid = int(want < cap ? want : cap);
         if (grid < 1) grid = 1;
-        if (dtype == MOE_B200_F16)
-            unpermute_kernel<MOE_B200_F16, 2, 4><<<grid, threads, 0, stream>>>(
-                static_cast<const uint4*>(y), packed_w, slot_pos, T, K, d / 8,
-                static_cast<uint4*>(out));
-        else
-            unpermute_kernel<MOE_B200_BF16, 2, 4><<<grid, threads, 0, stream>>>(
-                static_cast<const uint4*>(y), packed_w, slot_pos, T, K, d / 8,
-                static_cast<uint4*>(out));
+        cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(threads), 0, stream);
+        cudaLaunchAttribute attr = pdl_attr();
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        auto kern = dtype == MOE_B200_F16 ? unpermute_kernel<MOE_B200_F16, 2, 4>
+                                          : unpermute_kernel<MOE_B200_BF16, 2, 4>;
+        return cudaLaunchKernelEx(&cfg, kern, static_cast<const uint4*>(y), packed_w, slot_pos, T, K,
+                                  d / 8, static_cast<uint4*>(out));
     } else {
         int64_t n = int64_t(T) * d;
         int64_t want = (n + threads - 1) / threads;
-        int64_t cap = int64_t(sm_count_unperm()) * 32;
+        int64_t cap = int64_t(sms) * 32;
         int grid = int(want < cap ? want : cap);
         if (grid < 1) grid = 1;
-        if (dtype == MOE_B200_F16)
-            unpermute_scalar_kernel<MOE_B200_F16><<<grid, threads, 0, stream>>>(
-                static_cast<const uint16_t*>(y), packed_w, slot_pos, T, K, d,
-                static_cast<uint16_t*>(out));
-        else
-            unpermute_scalar_kernel<MOE_B200_BF16><<<grid, threads, 0, stream>>>(
-                static_cast<const uint16_t*>(y), packed_w, slot_pos, T, K, d,
-                static_cast<uint16_t*>(out));
+        cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(threads), 0, stream);
+        cudaLaunchAttribute attr = pdl_attr();
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        auto kern = dtype == MOE_B200_F16 ? unpermute_scalar_kernel<MOE_B200_F16>
+                                          : unpermute_scalar_kernel<MOE_B200_BF16>;
+        return cudaLaunchKernelEx(&cfg, kern, static_cast<const uint16_t*>(y), packed_w, slot_pos, T, K,
+                                  d, static_cast<uint16_t*>(out));
     }
     return cudaGetLastError();
 }

@@ -72,6 +72,8 @@ def lib() -> ctypes.CDLL:
                                 vp, vp, vp, vp, vp, vp, vp, sz, vp]
     L.moe_b200_workspace_status.restype = cint
     L.moe_b200_workspace_status.argtypes = [vp, sz, vp, ctypes.POINTER(cint)]
+    L.moe_b200_device_status.restype = cint
+    L.moe_b200_device_status.argtypes = [vp, ctypes.POINTER(cint)]
     L.moe_b200_unpermute.restype = cint
     L.moe_b200_unpermute.argtypes = [vp, vp, vp, cint, cint, cint, cint, vp, vp]
     _lib = L
@@ -254,6 +256,14 @@ def pack(emb, asgn, wts, E: int, workspace: Optional[Workspace] = None, out: Opt
         _ptr(out.expert_count), _ptr(out.expert_start), _ptr(out.slot_pos),
         workspace.buf.data_ptr(), workspace.nbytes, _stream_handle(stream)), "pack")
     return out
+
+
+def device_status(stream=None) -> int:
+    """Synchronise and return (and clear) the condition bits that workspace-less
+    kernels (unpermute, grouped FFN) recorded on the current device."""
+    out = ctypes.c_int(0)
+    _check(lib().moe_b200_device_status(_stream_handle(stream), ctypes.byref(out)), "device_status")
+    return out.value
 
 
 def dtype_code(torch_dtype) -> int:

@@ -12,8 +12,8 @@ One step = one pass of the hot path over one batch:
           unpermutes: weak scaling, value = all ranks' tokens / max-rank time.
 
 Prints ONE JSON line on rank 0.  `value` is device-timed (CUDA events on the
-launching stream, inputs resident in HBM, L2 flushed by a 256 MiB write before
-every step); `e2e` is the same metric through the C ABI with pinned host
+launching stream, inputs resident in HBM, L2 flushed by a 256 MiB write + a
+256 MiB read before every step); `e2e` is the same metric through the C ABI with pinned host
 buffers and the host<->device copies inside the timed region.
 """
 from __future__ import annotations
@@ -155,6 +155,28 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# ------------------------------------------------------------- L2 flush ----
+
+L2_NOTE = ("flushed before every step: 256 MiB write, then a 256 MiB read, so L2 holds none of "
+           "the step's data and no dirty lines")
+
+
+class L2Flush:
+    """Writes a 256 MiB buffer (2x the 126 MB L2), then reads another one so the
+    written lines are evicted (and written back) before the timed step starts."""
+
+    def __init__(self, dev):
+        import torch
+        self.w = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        self.r = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+        self.sink = torch.empty((), dtype=torch.float32, device=dev)
+
+    def __call__(self, i):
+        import torch
+        self.w.fill_(i & 0xFF)
+        torch.sum(self.r, dim=0, out=self.sink)
+
+
 # ----------------------------------------------------------- CPU legs -----
 
 def cpu_inputs(c, T_sample):
@@ -294,7 +316,7 @@ def gpu_arm(args):
 
     stream = torch.cuda.Stream(device=dev)
     warm = max(args.warmup, 3)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flusher = L2Flush(dev)
     with torch.cuda.stream(stream):
         ws = mb.Workspace(T, K, E, device=dev, stream=stream)
         bufs = mb.pack(emb, asgn, wts, E, workspace=ws, stream=stream)
@@ -307,12 +329,15 @@ def gpu_arm(args):
         recv_buf = torch.empty((world * TK, d), dtype=tdtype, device=dev)
         back_buf = torch.empty((TK, d), dtype=tdtype, device=dev)
 
-    def step():
-        """One pass; returns the op boundaries as events for the device timing."""
-        evs = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    def step(split=False):
+        """One pass.  Returns CUDA events recorded on the launching stream at the
+        step boundaries, plus one between pack and the rest when `split` (an
+        event there costs the PDL overlap, so the headline loop omits it)."""
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(3 if split else 2)]
         evs[0].record(stream)
         mb.pack(emb, asgn, wts, E, workspace=ws, out=bufs, stream=stream)
-        evs[1].record(stream)
+        if split:
+            evs[1].record(stream)
         y = bufs.packed
         if world > 1:
             starts = bufs.expert_start.long()
@@ -327,12 +352,12 @@ def gpu_arm(args):
             dist.all_to_all_single(back_buf, recv_buf[:nrecv], s_list, r_list)
             y = back_buf
         mb.unpermute(y, bufs.packed_weights, bufs.slot_pos, T, K, out=out, stream=stream)
-        evs[2].record(stream)
+        evs[-1].record(stream)
         return evs
 
     with torch.cuda.stream(stream):
-        for _ in range(warm):
-            flush.fill_(1)
+        for i in range(warm):
+            flusher(i)
             step()
         torch.cuda.synchronize(dev)
         assert ws.device_status(stream) == 0, "device-side condition during warm-up"
@@ -346,16 +371,24 @@ def gpu_arm(args):
         rec = []
         with ClockSampler(local) as clk:
             for i in range(args.steps):
-                flush.fill_(i & 0xFF)
+                flusher(i)
                 rec.append(step())
             torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
+        # attribution loop: the same steps with an event between pack and the rest
+        split = []
+        for i in range(args.steps):
+            flusher(i)
+            split.append(step(split=True))
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
 
-    pack_ms = [a.elapsed_time(b) for a, b, _ in rec]
-    rest_ms = [b.elapsed_time(cc) for _, b, cc in rec]
-    step_ms = [a.elapsed_time(cc) for a, _, cc in rec]
+    step_ms = [a.elapsed_time(b) for a, b in rec]
+    pack_ms = [a.elapsed_time(b) for a, b, _ in split]
+    rest_ms = [b.elapsed_time(cc) for _, b, cc in split]
     total_ms = sum(step_ms)
     if world > 1:
         t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
@@ -387,9 +420,11 @@ def gpu_arm(args):
             "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp16 rows (bitwise pack), fp32 combine accumulate",
             "data": "synthetic (seeded Gumbel top-K routing, N(0,1) rows)",
-            "config": config_json(c, world, "flushed before every step (256 MiB write)"),
+            "config": config_json(c, world, L2_NOTE),
             "hbm_gbs": (b_pack + b_unperm) / (ms / 1e3) / 1e9 if world == 1 else None,
-            "stages_ms": {"pack": mean_pack, "unpermute" if world == 1 else "dispatch+combine+unpermute": mean_rest},
+            "stages_ms": {"pack": mean_pack, "unpermute" if world == 1 else "dispatch+combine+unpermute": mean_rest,
+                          "note": "separate loop with an extra event between the stages (costs the "
+                                  "PDL overlap); the headline step has events at its boundaries only"},
             "roofline": {
                 "bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"
@@ -398,6 +433,7 @@ def gpu_arm(args):
                 "traffic": committed_traffic(traffic_key, c["name"]),
             },
             "gpu_launches": 3 * args.steps,
+            "kernels_per_step": ["route_scan_kernel", "pack_rows_bulk_kernel", "unpermute_bulk_kernel"],
             "clocks": clk.summary(),
         }
         if e2e is not None:
@@ -430,11 +466,11 @@ def e2e_leg(mb, c, emb_dev, asgn_np, wts_np, ws, stream, dev, steps, warm):
     d_wts = torch.empty((T, K), dtype=torch.float32, device=dev)
     d_out = torch.empty((T, d), dtype=emb_dev.dtype, device=dev)
     bufs = None
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flusher = L2Flush(dev)
     times = []
     with torch.cuda.stream(stream):
         for i in range(warm + steps):
-            flush.fill_(i & 0xFF)
+            flusher(i)
             a = torch.cuda.Event(enable_timing=True)
             b = torch.cuda.Event(enable_timing=True)
             a.record(stream)

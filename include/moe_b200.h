@@ -124,6 +124,12 @@ int moe_b200_pack_noalloc(const void* emb, const int32_t* asgn, const float* wts
                           int32_t* expert_count, int32_t* expert_start, int32_t* slot_pos,
                           void* stream);
 
+/* Synchronise `stream`, then read and clear the device-side condition bits
+ * (MOE_B200_DEV_*) that workspace-less kernels (unpermute, grouped FFN) of the
+ * current device recorded; *device_status = 0 means clean.  New: the
+ * reference reports nothing from the device.                               */
+int moe_b200_device_status(void* stream, int* device_status /* host */);
+
 /* ------------------------------------------------------------ combine ---- */
 
 /* Weighted unpermute + top-K combine:

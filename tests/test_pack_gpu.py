@@ -91,7 +91,9 @@ CASES = [
 
 
 @pytest.mark.parametrize("T,K,E,d,dist", CASES)
-def test_pack_matches_oracle(cuda, T, K, E, d, dist):
+@pytest.mark.parametrize("impl", ["bulk", "reg"])
+def test_pack_matches_oracle(cuda, T, K, E, d, dist, impl, monkeypatch):
+    monkeypatch.setenv("MOE_B200_PACK", impl)
     asgn, wts = routing.gen_routing(T, K, E, dist, seed=T + K)
     emb = np.random.default_rng(d).integers(0, 65536, (T, d), dtype=np.uint16)
     o = oracle.scatter(emb, asgn, wts, E)

@@ -37,7 +37,9 @@ def within_tol(got_u16, want_u16, dt, rtol):
                                      (1000, 3, 7, 24), (257, 2, 5, 20), (3000, 8, 128, 64),
                                      (700, 32, 40, 16)])
 @pytest.mark.parametrize("dt", [0, 1])
-def test_unpermute_matches_oracle(cuda, T, K, E, d, dt):
+@pytest.mark.parametrize("impl", ["bulk", "reg"])
+def test_unpermute_matches_oracle(cuda, T, K, E, d, dt, impl, monkeypatch):
+    monkeypatch.setenv("MOE_B200_UNPERMUTE", impl)
     tdt = torch.float16 if dt == 0 else torch.bfloat16
     asgn, wts = routing.gen_routing(T, K, E, "zipf", seed=T)
     rng = np.random.default_rng(T + d)
@@ -48,6 +50,7 @@ def test_unpermute_matches_oracle(cuda, T, K, E, d, dt):
     got = mb.unpermute(to_dev(y, tdt), torch.from_numpy(o["packed_weights"]).cuda(),
                        torch.from_numpy(o["slot_pos"]).cuda(), T, K)
     g = bits(got)
+    assert mb.device_status() == 0
     assert within_tol(g, want, dt, RTOL)
     assert g.tobytes() == want.tobytes()
 
