@@ -408,11 +408,11 @@ def gpu_arm(args):
         mean_rest = statistics.fmean(rest_ms)
         peak, peak_src = measured_peaks()
         if mean_rest >= mean_pack or world > 1:
-            dom, dom_bytes, dom_ms = "unpermute_kernel", b_unperm, mean_rest
+            dom, dom_bytes, dom_ms = "unpermute_bulk_kernel", b_unperm, mean_rest
         else:
-            dom, dom_bytes, dom_ms = "pack (route_scan_kernel + pack_rows_kernel)", b_pack, mean_pack
+            dom, dom_bytes, dom_ms = "pack (route_scan_kernel + pack_rows_bulk_kernel)", b_pack, mean_pack
         if world > 1:
-            dom, dom_bytes, dom_ms = "pack (route_scan_kernel + pack_rows_kernel)", b_pack, mean_pack
+            dom, dom_bytes, dom_ms = "pack (route_scan_kernel + pack_rows_bulk_kernel)", b_pack, mean_pack
         achieved = dom_bytes / (dom_ms / 1e3) / 1e9
         traffic_key = "unpermute_kernel" if dom.startswith("unpermute") else "pack"
         line = {
