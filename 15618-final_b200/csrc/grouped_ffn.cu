@@ -1,0 +1,508 @@
+// grouped_ffn.cu -- grouped SwiGLU expert FFN on the 5th-generation tensor
+// cores (tcgen05 + TMEM, TMA-fed), sm_100a.
+//
+//   h[r, :] = silu(x[r] . Wg[e]^T) * (x[r] . Wu[e]^T)     (GEMM 1, K = d)
+//   y[r, :] = h[r] . Wd[e]^T                               (GEMM 2, K = I)
+// for every packed row r of segment s, e = expert of s; fp32 accumulation in
+// TMEM, h and y rounded once to 16 bits.
+//
+// Replaces the reference's per-expert cublasHgemm loop (apps/bench_e2e.cu:
+// 274-301, apps/bench_prefill.cu:854-884) and its CUTLASS sm80 GemmGrouped
+// (apps/bench_prefill.cu:68-202, 812-852), both of which need the expert
+// counts on the host; here the tile list is derived on the device from the
+// segment offsets the packing kernel wrote.  The reference FFN has no
+// activation; this one is SwiGLU (gate, up, down).
+//
+// One persistent kernel, one CTA per SM, 6 warps:
+//   warp 0     TMA producer: A tile (128 rows x 64 K) + B tile (256 rows x 64 K)
+//              per stage, 128-byte swizzle, kStages stages
+//   warp 1     allocates TMEM (512 columns = two 128x256 fp32 accumulators)
+//              and issues tcgen05.mma (M=128, N=256, K=16) from one lane
+//   warps 2-5  epilogue: tcgen05.ld of their 32-lane quadrant, SwiGLU or
+//              plain conversion, 16-byte stores
+// Tiles are (segment, 128-row block, N block), N fastest, so concurrent CTAs
+// share the A block and the expert's weights in L2.  Every wait is bounded;
+// on expiry the CTA records MOE_B200_DEV_WAIT_TIMEOUT, raises a CTA-wide abort
+// flag so the other roles stop waiting, and still frees its TMEM.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace moe_b200 {
+
+constexpr int kTileM = 128;
+constexpr int kTileN = 256;
+constexpr int kTileK = 64;  // 64 x 16-bit = one 128-byte swizzle row
+constexpr int kStages = 4;
+constexpr int kFfnThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kABytes = kTileM * kTileK * 2;  // 16 KB
+constexpr uint32_t kBBytes = kTileN * kTileK * 2;  // 32 KB
+constexpr int kMaxSegments = 4096;  // keeps shared memory under 227 KB
+
+enum { kEpiSwiGLU = 0, kEpiStore = 1 };
+
+// ------------------------------------------------------------ tcgen05 -----
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
+// 128 bytes, 8-row groups 1024 bytes apart (SBO), version 1 (sm_100).
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= uint64_t((smem_addr >> 4) & 0x3FFF);  // start address
+    d |= uint64_t(1) << 16;                    // leading byte offset (unused for SW128 K-major)
+    d |= uint64_t(1024 >> 4) << 32;            // stride byte offset
+    d |= uint64_t(1) << 46;                    // descriptor version
+    d |= uint64_t(2) << 61;                    // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulate, A/B fp16 (0) or bf16
+// (1), both K-major, M = 128, N = 256.
+__host__ __device__ constexpr uint32_t umma_idesc(int ab_format) {
+    return (1u << 4) | (uint32_t(ab_format) << 7) | (uint32_t(ab_format) << 10) |
+           (uint32_t(kTileN >> 3) << 17) | (uint32_t(kTileM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive on an mbarrier once every tcgen05.mma issued so far by this thread
+// has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 2-D tiled TMA load (x = innermost coordinate in elements, y = row).
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y,
+                                           uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ------------------------------------------------------------ helpers -----
+
+template <int DT>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    if (DT == MOE_B200_BF16) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&v);
+    } else {
+        __half2 v = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.0f + __expf(-g)); }
+
+struct FfnSmem {
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    uint64_t tmem_full[2];
+    uint64_t tmem_empty[2];
+    uint32_t tmem_base;
+    int abort_flag;
+    int nseg;
+    int total_blocks;
+};
+
+// Bounded wait that also gives up as soon as another role raised the abort.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                              uint32_t* dev_status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            *abort_flag = 1;
+            atomicOr(dev_status, MOE_B200_DEV_WAIT_TIMEOUT);
+            return false;
+        }
+    }
+}
+
+// Maps a linear 128-row block index to (segment, block within segment).
+__device__ __forceinline__ int find_segment(const int32_t* blk_prefix, int nseg, int g) {
+    int lo = 0, hi = nseg - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (blk_prefix[mid] <= g) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+// EPI = kEpiSwiGLU: B rows of N block n are gate rows [n*128, n*128+128) and up
+// rows [I + n*128, ...) of the expert; the output has n_out = I columns.
+// EPI = kEpiStore: B rows [n*256, n*256+256) of the expert; n_out columns.
+template <int EPI, int DT>
+__global__ void __launch_bounds__(kFfnThreads, 1)
+grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                    const int32_t* __restrict__ seg_start, const int32_t* __restrict__ seg_expert,
+                    int nseg, int kdim, int b_rows_per_expert, int n_out, int n_blocks,
+                    int gate_up_split, uint16_t* __restrict__ out, int64_t out_stride,
+                    uint32_t* __restrict__ dev_status) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // 1024-byte aligned stage buffers (SW128 atoms), control block after them.
+    unsigned char* base = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* sA = base;
+    unsigned char* sB = base + kStages * kABytes;
+    FfnSmem* ctl = reinterpret_cast<FfnSmem*>(sB + kStages * kBBytes);
+    int32_t* blk_prefix = reinterpret_cast<int32_t*>(ctl + 1);  // [nseg + 1]
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    volatile int* abort_flag = &ctl->abort_flag;
+
+    // Set-up: barriers, block prefix over segments, TMEM.
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&ctl->full[s], 1);
+            mbar_init(&ctl->empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&ctl->tmem_full[b], 1);
+            mbar_init(&ctl->tmem_empty[b], 4);
+        }
+        ctl->abort_flag = 0;
+        mbar_fence_init();
+    }
+    if (warp == 0) {
+        // blk_prefix[s] = number of 128-row blocks in segments < s
+        int run = 0;
+        for (int s0 = 0; s0 < nseg; s0 += 32) {
+            int s = s0 + lane;
+            int cnt = 0;
+            if (s < nseg) {
+                int rows = seg_start[s + 1] - seg_start[s];
+                cnt = rows > 0 ? (rows + kTileM - 1) / kTileM : 0;
+            }
+            int incl = cnt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            if (s < nseg) blk_prefix[s] = run + incl - cnt;
+            run += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) {
+            blk_prefix[nseg] = run;
+            ctl->total_blocks = run;
+        }
+        if (lane == 0) {
+            prefetch_tmap(&tmap_a);
+            prefetch_tmap(&tmap_b);
+        }
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&ctl->tmem_base)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    const uint32_t tmem = ctl->tmem_base;
+    const int total_tiles = ctl->total_blocks * n_blocks;
+    const int nk = (kdim + kTileK - 1) / kTileK;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
+                const int g = tile / n_blocks, n = tile % n_blocks;
+                const int s = find_segment(blk_prefix, nseg, g);
+                const int e = seg_expert ? seg_expert[s] : s;
+                const int row0 = seg_start[s] + (g - blk_prefix[s]) * kTileM;
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int st = int(it % kStages);
+                    if (!wait_or_abort(&ctl->empty[st], ((it / kStages) & 1u) ^ 1u, abort_flag, dev_status))
+                        break;
+                    mbar_arrive_expect_tx(&ctl->full[st], kABytes + kBBytes);
+                    tma_load_2d(sA + st * kABytes, &tmap_a, kb * kTileK, row0, &ctl->full[st]);
+                    unsigned char* b = sB + st * kBBytes;
+                    if (EPI == kEpiSwiGLU) {
+                        const int brow = e * b_rows_per_expert + n * (kTileN / 2);
+                        tma_load_2d(b, &tmap_b, kb * kTileK, brow, &ctl->full[st]);
+                        tma_load_2d(b + kBBytes / 2, &tmap_b, kb * kTileK, brow + gate_up_split,
+                                    &ctl->full[st]);
+                    } else {
+                        tma_load_2d(b, &tmap_b, kb * kTileK, e * b_rows_per_expert + n * kTileN,
+                                    &ctl->full[st]);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc(DT == MOE_B200_BF16 ? 1 : 0);
+            uint32_t it = 0, j = 0;
+            for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x, ++j) {
+                const int buf = int(j & 1u);
+                if (!wait_or_abort(&ctl->tmem_empty[buf], ((j >> 1) & 1u) ^ 1u, abort_flag, dev_status))
+                    break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + uint32_t(buf) * kTileN;
+                bool ok = true;
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int st = int(it % kStages);
+                    if (!wait_or_abort(&ctl->full[st], (it / kStages) & 1u, abort_flag, dev_status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sA + st * kABytes);
+                    const uint32_t b_addr = smem_u32(sB + st * kBBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kTileK / 16; ++kk) {
+                        // +32 bytes per 16-element K step inside the 128-byte swizzle row
+                        umma_f16(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32),
+                                 idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&ctl->empty[st]);
+                }
+                if (!ok) break;
+                umma_commit(&ctl->tmem_full[buf]);
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
+        const int r_in_tile = quad * 32 + lane;
+        uint32_t j = 0;
+        for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++j) {
+            const int buf = int(j & 1u);
+            if (!wait_or_abort(&ctl->tmem_full[buf], (j >> 1) & 1u, abort_flag, dev_status)) break;
+            tc_fence_after();
+            const int g = tile / n_blocks, n = tile % n_blocks;
+            const int s = find_segment(blk_prefix, nseg, g);
+            const int blk = g - blk_prefix[s];
+            const int seg_rows = seg_start[s + 1] - seg_start[s];
+            const bool row_ok = blk * kTileM + r_in_tile < seg_rows;
+            const int64_t row = int64_t(seg_start[s]) + blk * kTileM + r_in_tile;
+            const uint32_t t_row = tmem + uint32_t(buf) * kTileN + (uint32_t(quad * 32) << 16);
+            if (EPI == kEpiSwiGLU) {
+#pragma unroll 1
+                for (int c = 0; c < kTileN / 2; c += 16) {
+                    uint32_t gr[16], ur[16];
+                    tmem_ld16(t_row + c, gr);
+                    tmem_ld16(t_row + kTileN / 2 + c, ur);
+                    tmem_wait_ld();
+                    const int col = n * (kTileN / 2) + c;
+                    if (row_ok && col < n_out) {
+                        uint32_t o[8];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const float g0 = __uint_as_float(gr[2 * q]), g1 = __uint_as_float(gr[2 * q + 1]);
+                            const float u0 = __uint_as_float(ur[2 * q]), u1 = __uint_as_float(ur[2 * q + 1]);
+                            o[q] = pack2<DT>(silu(g0) * u0, silu(g1) * u1);
+                        }
+                        uint4* dst = reinterpret_cast<uint4*>(out + row * out_stride + col);
+                        if (col + 16 <= n_out) {
+                            st_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
+                            st_v4(dst + 1, make_uint4(o[4], o[5], o[6], o[7]));
+                        } else if (col + 8 <= n_out) {
+                            st_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
+                        }
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < kTileN; c += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(t_row + c, v);
+                    tmem_wait_ld();
+                    const int col = n * kTileN + c;
+                    if (row_ok && col < n_out) {
+                        uint32_t o[8];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            o[q] = pack2<DT>(__uint_as_float(v[2 * q]), __uint_as_float(v[2 * q + 1]));
+                        uint4* dst = reinterpret_cast<uint4*>(out + row * out_stride + col);
+                        if (col + 16 <= n_out) {
+                            st_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
+                            st_v4(dst + 1, make_uint4(o[4], o[5], o[6], o[7]));
+                        } else if (col + 8 <= n_out) {
+                            st_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->tmem_empty[buf]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
+// ----------------------------------------------------------------- host ----
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2-D K-major map over a row-major [rows, cols] 16-bit matrix; box = 64 x box_rows, 128B swizzle.
+static bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows,
+                     int dtype) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(cols) * 2};
+    cuuint32_t box[2] = {cuuint32_t(kTileK), cuuint32_t(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, dtype == MOE_B200_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                    2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+static size_t ffn_smem_bytes(int nseg) {
+    return 1024 + kStages * (kABytes + kBBytes) + sizeof(FfnSmem) + size_t(nseg + 1) * 4;
+}
+
+static int sm_count_ffn() {
+    int dev = 0, n = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+template <int EPI, int DT>
+static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb_, const int32_t* seg_start,
+                               const int32_t* seg_expert, int nseg, int rows, int kdim, int b_rows_per_expert,
+                               int n_out, int n_blocks, int split, void* out, int64_t out_stride,
+                               uint32_t* st, cudaStream_t stream) {
+    const size_t smem = ffn_smem_bytes(nseg);
+    auto kern = grouped_gemm_kernel<EPI, DT>;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (err != cudaSuccess) return err;
+    // Upper bound on tiles: every segment may add one partial block.
+    const int64_t max_tiles = (int64_t(rows) / kTileM + nseg) * n_blocks;
+    int grid = sm_count_ffn();
+    if (max_tiles < grid) grid = int(max_tiles > 0 ? max_tiles : 1);
+    cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(kFfnThreads), smem, stream);
+    return cudaLaunchKernelEx(&cfg, kern, ma, mb_, seg_start, seg_expert, nseg, kdim, b_rows_per_expert, n_out,
+                              n_blocks, split, static_cast<uint16_t*>(out), out_stride, st);
+}
+
+int fail(int code, const char* fmt, ...);
+int cuda_fail(cudaError_t err, const char* where);
+
+}  // namespace moe_b200
+
+extern "C" int moe_b200_grouped_swiglu(const void* x, const int32_t* seg_start, const int32_t* seg_expert,
+                                       int nseg, int rows, int d, int I, int E, const void* w_gate_up,
+                                       const void* w_down, int dtype, void* h, void* y, void* stream) {
+    using namespace moe_b200;
+    if (nseg < 1 || rows < 0 || d < 1 || I < 1 || E < 1)
+        return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: need nseg>=1, rows>=0, d>=1, I>=1, E>=1");
+    if (nseg > kMaxSegments)
+        return fail(MOE_B200_ERR_UNSUPPORTED, "grouped_swiglu: %d segments exceed %d", nseg, kMaxSegments);
+    if (dtype != MOE_B200_F16 && dtype != MOE_B200_BF16)
+        return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: dtype %d is neither F16 nor BF16", dtype);
+    if (d % 16 != 0 || I % 16 != 0)
+        return fail(MOE_B200_ERR_UNSUPPORTED, "grouped_swiglu: d and I must be multiples of 16 (d=%d I=%d)", d, I);
+    if (!x || !seg_start || !w_gate_up || !w_down || !h || !y)
+        return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: null pointer");
+    const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w_gate_up) |
+                         reinterpret_cast<uintptr_t>(w_down) | reinterpret_cast<uintptr_t>(h) |
+                         reinterpret_cast<uintptr_t>(y);
+    if (al % 16 != 0) return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: pointers must be 16-byte aligned");
+    if (rows == 0) return MOE_B200_OK;
+    uint32_t* st = device_status_word();
+    if (!st) return fail(MOE_B200_ERR_CUDA, "grouped_swiglu: device status word unavailable");
+    CUtensorMap mx, mwgu, mh, mwd;
+    if (!make_map(&mx, x, rows, d, kTileM, dtype) ||
+        !make_map(&mwgu, w_gate_up, int64_t(E) * 2 * I, d, kTileN / 2, dtype) ||
+        !make_map(&mh, h, rows, I, kTileM, dtype) ||
+        !make_map(&mwd, w_down, int64_t(E) * d, I, kTileN, dtype))
+        return fail(MOE_B200_ERR_CUDA, "grouped_swiglu: cuTensorMapEncodeTiled failed");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int nb1 = (I + kTileN / 2 - 1) / (kTileN / 2);
+    const int nb2 = (d + kTileN - 1) / kTileN;
+    cudaError_t err;
+    if (dtype == MOE_B200_BF16) {
+        err = launch_gemm<kEpiSwiGLU, MOE_B200_BF16>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1,
+                                                     I, h, I, st, s);
+        if (err == cudaSuccess)
+            err = launch_gemm<kEpiStore, MOE_B200_BF16>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0,
+                                                        y, d, st, s);
+    } else {
+        err = launch_gemm<kEpiSwiGLU, MOE_B200_F16>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1,
+                                                    I, h, I, st, s);
+        if (err == cudaSuccess)
+            err = launch_gemm<kEpiStore, MOE_B200_F16>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0,
+                                                       y, d, st, s);
+    }
+    return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "grouped_swiglu launch");
+}

@@ -74,6 +74,8 @@ def lib() -> ctypes.CDLL:
     L.moe_b200_workspace_status.argtypes = [vp, sz, vp, ctypes.POINTER(cint)]
     L.moe_b200_device_status.restype = cint
     L.moe_b200_device_status.argtypes = [vp, ctypes.POINTER(cint)]
+    L.moe_b200_grouped_swiglu.restype = cint
+    L.moe_b200_grouped_swiglu.argtypes = [vp, vp, vp, cint, cint, cint, cint, cint, vp, vp, cint, vp, vp, vp]
     L.moe_b200_unpermute.restype = cint
     L.moe_b200_unpermute.argtypes = [vp, vp, vp, cint, cint, cint, cint, vp, vp]
     _lib = L
@@ -285,3 +287,22 @@ def unpermute(y, packed_weights, slot_pos, T: int, K: int, out=None, stream=None
                                     dtype_code(y.dtype), _ptr(out), _stream_handle(stream)),
            "unpermute")
     return out
+
+
+def grouped_swiglu(x, seg_start, w_gate_up, w_down, seg_expert=None, h=None, y=None, stream=None):
+    """Grouped SwiGLU FFN over packed rows x [rows, d] (bf16/fp16).
+    seg_start: int32 [nseg + 1] device offsets (e.g. expert_start from pack);
+    w_gate_up [E, 2I, d], w_down [E, d, I].  Returns (h [rows, I], y [rows, d])."""
+    import torch
+    rows, d = x.shape
+    E, two_i, _ = w_gate_up.shape
+    I = two_i // 2
+    nseg = seg_start.numel() - 1
+    if h is None:
+        h = torch.empty((rows, I), dtype=x.dtype, device=x.device)
+    if y is None:
+        y = torch.empty((rows, d), dtype=x.dtype, device=x.device)
+    _check(lib().moe_b200_grouped_swiglu(_ptr(x), _ptr(seg_start), _ptr(seg_expert), nseg, rows, d, I, E,
+                                         _ptr(w_gate_up), _ptr(w_down), dtype_code(x.dtype), _ptr(h), _ptr(y),
+                                         _stream_handle(stream)), "grouped_swiglu")
+    return h, y

@@ -140,6 +140,29 @@ int moe_b200_device_status(void* stream, int* device_status /* host */);
 int moe_b200_unpermute(const void* y, const float* packed_weights, const int32_t* slot_pos,
                        int T, int K, int d, int dtype, void* out, void* stream);
 
+/* ---------------------------------------------------------- expert FFN ---- */
+
+/* Grouped SwiGLU expert FFN on packed rows, on the tcgen05 tensor cores:
+ *   h[r] = silu(x[r] . Wg[e]^T) * (x[r] . Wu[e]^T),   y[r] = h[r] . Wd[e]^T
+ * for each row r of segment s (rows [seg_start[s], seg_start[s+1])), with
+ * e = seg_expert[s] (seg_expert NULL: e = s, e.g. seg_start = expert_start
+ * from moe_b200_pack).  fp32 accumulation; h and y rounded once to dtype.
+ *   x          [rows, d]       packed rows (16-bit, dtype)
+ *   w_gate_up  [E, 2*I, d]     row j < I: gate column j; row I + j: up column j
+ *   w_down     [E, d, I]       row c: output column c over the I inner features
+ *   h          [rows, I]       out: the SwiGLU intermediate
+ *   y          [rows, d]       out: expert outputs, in packed order
+ * d and I multiples of 16; all pointers 16-byte aligned; nseg <= 4096.
+ * Replaces the per-expert cublasHgemm loop (apps/bench_e2e.cu:274-301,
+ * apps/bench_prefill.cu:854-884) and the CUTLASS sm80 GemmGrouped FFN
+ * (apps/bench_prefill.cu:68-202, 812-852), which have no activation and need
+ * the expert counts on the host.  Device-side conditions are reported by
+ * moe_b200_device_status().                                                 */
+int moe_b200_grouped_swiglu(const void* x, const int32_t* seg_start, const int32_t* seg_expert,
+                            int nseg, int rows, int d, int I, int E,
+                            const void* w_gate_up, const void* w_down, int dtype,
+                            void* h, void* y, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif
