@@ -43,7 +43,7 @@ constexpr int kFfnThreads = 192;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kABytes = kTileM * kTileK * 2;  // 16 KB
 constexpr uint32_t kBBytes = kTileN * kTileK * 2;  // 32 KB
-constexpr int kMaxSegments = 4096;  // keeps shared memory under 227 KB
+constexpr int kMaxSegments = 2048;  // keeps shared memory under 227 KB
 
 enum { kEpiSwiGLU = 0, kEpiStore = 1 };
 
@@ -191,6 +191,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     unsigned char* sB = base + kStages * kABytes;
     FfnSmem* ctl = reinterpret_cast<FfnSmem*>(sB + kStages * kBBytes);
     int32_t* blk_prefix = reinterpret_cast<int32_t*>(ctl + 1);  // [nseg + 1]
+    int32_t* s_start = blk_prefix + (nseg + 1);                 // [nseg + 1] row offsets
+    int32_t* s_expert = s_start + (nseg + 1);                   // [nseg] expert of each segment
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     volatile int* abort_flag = &ctl->abort_flag;
@@ -215,7 +217,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             int s = s0 + lane;
             int cnt = 0;
             if (s < nseg) {
-                int rows = seg_start[s + 1] - seg_start[s];
+                const int lo = seg_start[s], hi = seg_start[s + 1];
+                s_start[s] = lo;
+                s_expert[s] = seg_expert ? seg_expert[s] : s;
+                int rows = hi - lo;
                 cnt = rows > 0 ? (rows + kTileM - 1) / kTileM : 0;
             }
             int incl = cnt;
@@ -229,6 +234,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         }
         if (lane == 0) {
             blk_prefix[nseg] = run;
+            s_start[nseg] = seg_start[nseg];
             ctl->total_blocks = run;
         }
         if (lane == 0) {
@@ -258,8 +264,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
                 const int g = tile / n_blocks, n = tile % n_blocks;
                 const int s = find_segment(blk_prefix, nseg, g);
-                const int e = seg_expert ? seg_expert[s] : s;
-                const int row0 = seg_start[s] + (g - blk_prefix[s]) * kTileM;
+                const int e = s_expert[s];
+                const int row0 = s_start[s] + (g - blk_prefix[s]) * kTileM;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const int st = int(it % kStages);
                     if (!wait_or_abort(&ctl->empty[st], ((it / kStages) & 1u) ^ 1u, abort_flag, dev_status))
@@ -324,53 +330,56 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             const int g = tile / n_blocks, n = tile % n_blocks;
             const int s = find_segment(blk_prefix, nseg, g);
             const int blk = g - blk_prefix[s];
-            const int seg_rows = seg_start[s + 1] - seg_start[s];
+            const int seg_rows = s_start[s + 1] - s_start[s];
             const bool row_ok = blk * kTileM + r_in_tile < seg_rows;
-            const int64_t row = int64_t(seg_start[s]) + blk * kTileM + r_in_tile;
+            const int64_t row = int64_t(s_start[s]) + blk * kTileM + r_in_tile;
             const uint32_t t_row = tmem + uint32_t(buf) * kTileN + (uint32_t(quad * 32) << 16);
             if (EPI == kEpiSwiGLU) {
+                // 32 gate + 32 up columns per TMEM round trip
 #pragma unroll 1
-                for (int c = 0; c < kTileN / 2; c += 16) {
-                    uint32_t gr[16], ur[16];
-                    tmem_ld16(t_row + c, gr);
-                    tmem_ld16(t_row + kTileN / 2 + c, ur);
+                for (int c = 0; c < kTileN / 2; c += 32) {
+                    uint32_t gr[2][16], ur[2][16];
+                    tmem_ld16(t_row + c, gr[0]);
+                    tmem_ld16(t_row + c + 16, gr[1]);
+                    tmem_ld16(t_row + kTileN / 2 + c, ur[0]);
+                    tmem_ld16(t_row + kTileN / 2 + c + 16, ur[1]);
                     tmem_wait_ld();
-                    const int col = n * (kTileN / 2) + c;
-                    if (row_ok && col < n_out) {
-                        uint32_t o[8];
 #pragma unroll
-                        for (int q = 0; q < 8; ++q) {
-                            const float g0 = __uint_as_float(gr[2 * q]), g1 = __uint_as_float(gr[2 * q + 1]);
-                            const float u0 = __uint_as_float(ur[2 * q]), u1 = __uint_as_float(ur[2 * q + 1]);
-                            o[q] = pack2<DT>(silu(g0) * u0, silu(g1) * u1);
-                        }
-                        uint4* dst = reinterpret_cast<uint4*>(out + row * out_stride + col);
-                        if (col + 16 <= n_out) {
+                    for (int hb = 0; hb < 2; ++hb) {
+                        const int col = n * (kTileN / 2) + c + hb * 16;
+                        if (row_ok && col < n_out) {
+                            uint32_t o[8];
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                const float g0 = __uint_as_float(gr[hb][2 * q]), g1 = __uint_as_float(gr[hb][2 * q + 1]);
+                                const float u0 = __uint_as_float(ur[hb][2 * q]), u1 = __uint_as_float(ur[hb][2 * q + 1]);
+                                o[q] = pack2<DT>(silu(g0) * u0, silu(g1) * u1);
+                            }
+                            uint4* dst = reinterpret_cast<uint4*>(out + row * out_stride + col);
                             st_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
                             st_v4(dst + 1, make_uint4(o[4], o[5], o[6], o[7]));
-                        } else if (col + 8 <= n_out) {
-                            st_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
                         }
                     }
                 }
             } else {
+                // 64 columns per TMEM round trip
 #pragma unroll 1
-                for (int c = 0; c < kTileN; c += 16) {
-                    uint32_t v[16];
-                    tmem_ld16(t_row + c, v);
-                    tmem_wait_ld();
-                    const int col = n * kTileN + c;
-                    if (row_ok && col < n_out) {
-                        uint32_t o[8];
+                for (int c = 0; c < kTileN; c += 64) {
+                    uint32_t v[4][16];
 #pragma unroll
-                        for (int q = 0; q < 8; ++q)
-                            o[q] = pack2<DT>(__uint_as_float(v[2 * q]), __uint_as_float(v[2 * q + 1]));
-                        uint4* dst = reinterpret_cast<uint4*>(out + row * out_stride + col);
-                        if (col + 16 <= n_out) {
+                    for (int q4 = 0; q4 < 4; ++q4) tmem_ld16(t_row + c + 16 * q4, v[q4]);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        const int col = n * kTileN + c + 16 * q4;
+                        if (row_ok && col < n_out) {
+                            uint32_t o[8];
+#pragma unroll
+                            for (int q = 0; q < 8; ++q)
+                                o[q] = pack2<DT>(__uint_as_float(v[q4][2 * q]), __uint_as_float(v[q4][2 * q + 1]));
+                            uint4* dst = reinterpret_cast<uint4*>(out + row * out_stride + col);
                             st_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
                             st_v4(dst + 1, make_uint4(o[4], o[5], o[6], o[7]));
-                        } else if (col + 8 <= n_out) {
-                            st_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
                         }
                     }
                 }
@@ -428,7 +437,7 @@ static bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t c
 }
 
 static size_t ffn_smem_bytes(int nseg) {
-    return 1024 + kStages * (kABytes + kBBytes) + sizeof(FfnSmem) + size_t(nseg + 1) * 4;
+    return 1024 + kStages * (kABytes + kBBytes) + sizeof(FfnSmem) + size_t(3 * nseg + 2) * 4;
 }
 
 static int sm_count_ffn() {

@@ -112,7 +112,7 @@ unpermute_kernel(const uint4* __restrict__ y, const float* __restrict__ packed_w
 // stage; the consumers wait on the stage's mbarrier, accumulate the K rows in
 // fp32 (ascending k, one FMA per term), round once and store the output row.
 // `stages` stages per CTA keep stages*K rows in flight with no register cost.
-constexpr int kConsumerWarps = 4;
+constexpr int kConsumerWarps = 8;
 constexpr int kBulkThreads = (kConsumerWarps + 1) * 32;
 
 template <int DT>
@@ -149,22 +149,23 @@ unpermute_bulk_kernel(const uint16_t* __restrict__ y, const float* __restrict__ 
         const int gk = lane % K, gi = lane / K;
         const bool lane_used = gi < G;
         const int64_t n_mine = (T - 1 - int64_t(blockIdx.x)) / gridDim.x + 1;  // tokens of this CTA
-        auto fetch = [&](int64_t g, int32_t& p, float& w) {
+        auto fetch_p = [&](int64_t g) -> int32_t {
             const int64_t i = g * G + gi;
-            p = -1;
-            w = 0.f;
-            if (lane_used && i < n_mine) {
-                const int64_t t = int64_t(blockIdx.x) + i * gridDim.x;
-                p = __ldg(slot_pos + t * K + gk);
-                if (p >= 0) w = __ldg(packed_w + p);
-            }
+            if (!lane_used || i >= n_mine) return -1;
+            const int64_t t = int64_t(blockIdx.x) + i * gridDim.x;
+            return __ldg(slot_pos + t * K + gk);
         };
-        int32_t p_cur, p_nxt;
-        float w_cur, w_nxt;
-        fetch(0, p_cur, w_cur);
+        auto fetch_w = [&](int32_t p) -> float { return p >= 0 ? __ldg(packed_w + p) : 0.f; };
+        // indices run two groups ahead, weights one group ahead, so no
+        // dependent load sits on the per-group path
+        int32_t p_cur = fetch_p(0);
+        int32_t p_nxt = fetch_p(1);
+        float w_cur = fetch_w(p_cur);
+        float w_nxt;
         bool ok = true;
         for (int64_t g = 0; ok && g * G < n_mine; ++g) {
-            fetch(g + 1, p_nxt, w_nxt);
+            const int32_t p_nn = fetch_p(g + 2);
+            w_nxt = fetch_w(p_nxt);
             for (int q = 0; q < G; ++q) {
                 const int64_t i = g * G + q;
                 if (i >= n_mine) break;
@@ -190,6 +191,7 @@ unpermute_bulk_kernel(const uint16_t* __restrict__ y, const float* __restrict__ 
             }
             p_cur = p_nxt;
             w_cur = w_nxt;
+            p_nxt = p_nn;
         }
     } else {
         const int ctid = tid;  // 0 .. 32*kConsumerWarps-1

@@ -10,7 +10,7 @@ packed[expert_start[lo_g] : expert_start[hi_g]].
 """
 from __future__ import annotations
 
-from typing import List
+from typing import List, NamedTuple
 
 
 def expert_ranges(E: int, N: int) -> List[int]:
@@ -52,3 +52,92 @@ def recv_layout(all_counts, bounds, rank):
             segs.append((g, e, off, c))
             off += c
     return recv, segs
+
+
+def layout_reference(all_counts, rank, bounds):
+    """Host restatement of moe_b200_ep_layout (used to check it and in CPU
+    tests): (seg_start, seg_expert, send_counts, recv_counts) as lists."""
+    N = len(all_counts)
+    lo, hi = bounds[rank], bounds[rank + 1]
+    send = [sum(int(all_counts[rank][e]) for e in range(bounds[g], bounds[g + 1])) for g in range(N)]
+    recv, segs = recv_layout(all_counts, bounds, rank)
+    seg_start = [s[2] for s in segs] + [sum(recv)]
+    seg_expert = [s[1] - lo for s in segs]
+    return seg_start, seg_expert, send, recv
+
+
+class Layout(NamedTuple):
+    seg_start: object     # device int32 [N*L + 1]
+    seg_expert: object    # device int32 [N*L]
+    send: List[int]       # rows sent to each rank (host)
+    recv: List[int]       # rows received from each rank (host)
+
+
+class ExpertParallel:
+    """Dispatch / combine of packed rows across expert-parallel ranks, one
+    process per GPU, over torch.distributed (NCCL on GPUs).
+
+    dispatch: one all-gather of the E expert counts, the layout on the device
+    (moe_b200_ep_layout), ONE device-to-host copy of the 2N split sizes (the
+    collective library needs them on the host, as the reference's
+    ncclSend/ncclRecv loop does, apps/bench_prefill.cu:768-807), then one
+    AllToAllv of the rows.  The packed buffer is the send buffer.
+    combine: the reverse AllToAllv, back into the sender's packed order
+    (apps/bench_prefill.cu:889-906).
+
+    `layout_fn(all_counts, rank, bounds)` may replace the device layout (the
+    CPU tests inject layout_reference); by default the CUDA kernel runs."""
+
+    def __init__(self, E: int, group=None, device=None, layout_fn=None):
+        import torch
+        import torch.distributed as dist
+        self.dist = dist
+        self.group = group
+        self.N = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.E = E
+        self.bounds = expert_ranges(E, self.N)
+        self.L = self.bounds[self.rank + 1] - self.bounds[self.rank]
+        self.device = device
+        self.all_counts = torch.empty((self.N, E), dtype=torch.int32, device=device)
+        self.layout_fn = layout_fn
+
+    def exchange_counts(self, expert_count):
+        self.dist.all_gather_into_tensor(self.all_counts.view(-1), expert_count[: self.E].contiguous(),
+                                         group=self.group)
+        return self.all_counts
+
+    def layout(self, expert_count) -> Layout:
+        import torch
+        counts = self.exchange_counts(expert_count)
+        if self.layout_fn is None:
+            import moe_b200 as mb
+            seg_start, seg_expert, send, recv = mb.ep_layout(counts, self.rank, self.bounds)
+            host = torch.stack([send, recv]).cpu()
+            return Layout(seg_start, seg_expert, host[0].tolist(), host[1].tolist())
+        ss, se, send, recv = self.layout_fn(counts.cpu().tolist(), self.rank, self.bounds)
+        return Layout(torch.tensor(ss, dtype=torch.int32, device=self.device),
+                      torch.tensor(se, dtype=torch.int32, device=self.device), send, recv)
+
+    def dispatch(self, packed, expert_count, recv_buf=None):
+        """Returns (rows received [sum(recv), d] in sender-major / expert-major
+        order, layout)."""
+        import torch
+        lay = self.layout(expert_count)
+        nrecv = sum(lay.recv)
+        if recv_buf is None or recv_buf.shape[0] < nrecv:
+            recv_buf = torch.empty((nrecv, packed.shape[1]), dtype=packed.dtype, device=packed.device)
+        out = recv_buf[:nrecv]
+        self.dist.all_to_all_single(out, packed[: sum(lay.send)], lay.recv, lay.send, group=self.group)
+        return out, lay
+
+    def combine(self, y, lay: Layout, back=None):
+        """Sends expert outputs y (receive order) back; returns rows aligned with
+        this rank's packed buffer."""
+        import torch
+        nsend = sum(lay.send)
+        if back is None or back.shape[0] < nsend:
+            back = torch.empty((nsend, y.shape[1]), dtype=y.dtype, device=y.device)
+        out = back[:nsend]
+        self.dist.all_to_all_single(out, y[: sum(lay.recv)], lay.send, lay.recv, group=self.group)
+        return out

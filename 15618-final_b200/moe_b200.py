@@ -76,6 +76,8 @@ def lib() -> ctypes.CDLL:
     L.moe_b200_device_status.argtypes = [vp, ctypes.POINTER(cint)]
     L.moe_b200_grouped_swiglu.restype = cint
     L.moe_b200_grouped_swiglu.argtypes = [vp, vp, vp, cint, cint, cint, cint, cint, vp, vp, cint, vp, vp, vp]
+    L.moe_b200_ep_layout.restype = cint
+    L.moe_b200_ep_layout.argtypes = [vp, cint, cint, cint, ctypes.POINTER(ctypes.c_int32), vp, vp, vp, vp, vp]
     L.moe_b200_unpermute.restype = cint
     L.moe_b200_unpermute.argtypes = [vp, vp, vp, cint, cint, cint, cint, vp, vp]
     _lib = L
@@ -306,3 +308,23 @@ def grouped_swiglu(x, seg_start, w_gate_up, w_down, seg_expert=None, h=None, y=N
                                          _ptr(w_gate_up), _ptr(w_down), dtype_code(x.dtype), _ptr(h), _ptr(y),
                                          _stream_handle(stream)), "grouped_swiglu")
     return h, y
+
+
+def ep_layout(all_counts, rank, expert_first, out=None, stream=None):
+    """Device-side EP layout from all_counts [N, E] (int32, device).
+    Returns (seg_start [N*L+1], seg_expert [N*L], send_counts [N], recv_counts [N])."""
+    import torch
+    N, E = all_counts.shape
+    if not (0 <= rank < N) or len(expert_first) != N + 1:
+        raise MoEB200Error(ERR_INVALID_ARG, f"ep_layout: rank {rank} / {len(expert_first)} bounds for {N} ranks")
+    L = expert_first[rank + 1] - expert_first[rank]
+    dev = all_counts.device
+    if out is None:
+        out = (torch.empty(N * L + 1, dtype=torch.int32, device=dev),
+               torch.empty(max(N * L, 1), dtype=torch.int32, device=dev),
+               torch.empty(N, dtype=torch.int32, device=dev),
+               torch.empty(N, dtype=torch.int32, device=dev))
+    first = (ctypes.c_int32 * (N + 1))(*expert_first)
+    _check(lib().moe_b200_ep_layout(_ptr(all_counts), N, E, rank, first, _ptr(out[0]), _ptr(out[1]),
+                                    _ptr(out[2]), _ptr(out[3]), _stream_handle(stream)), "ep_layout")
+    return out

@@ -35,6 +35,7 @@ import numpy as np  # noqa: E402
 import routing  # noqa: E402
 
 METRIC = "scatter+unpermute tokens/s"
+METRIC_LAYER = "EP MoE layer us"
 UNIT = "tokens/s"
 FALLBACK_HBM_GBS = 6650.0
 
@@ -45,7 +46,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4"])
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -86,6 +87,16 @@ def measured_peaks():
         return float(p["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_tflops():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), "measured burst bf16 (MEASURED_PEAKS.json bf16_tflops)"
+    except Exception:
+        return 1590.0, "fallback 1.59 PFLOP/s"
 
 
 def committed_traffic(kernel, workload_name):
@@ -292,6 +303,7 @@ def gpu_arm(args):
     import torch
     import torch.distributed as dist
     import moe_b200 as mb
+    import ep
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -306,6 +318,12 @@ def gpu_arm(args):
 
     c = workload(args.config, rank)
     c["name"] = args.config
+    layer = "I" in c                       # c5: the full layer with SwiGLU experts
+    if layer:
+        # the layer's T tokens are split over the ranks (apps/bench_prefill.cu:341)
+        if c["T"] % world:
+            raise SystemExit(f"T={c['T']} not divisible by {world} ranks")
+        c["T"] = c["T"] // world
     T, K, E, d = c["T"], c["K"], c["E"], c["d"]
     TK = T * K
     tdtype = getattr(torch, c["dtype"])
@@ -317,40 +335,57 @@ def gpu_arm(args):
     stream = torch.cuda.Stream(device=dev)
     warm = max(args.warmup, 3)
     flusher = L2Flush(dev)
+    bounds = ep.expert_ranges(E, world)
+    lo, hi = bounds[rank], bounds[rank + 1]
     with torch.cuda.stream(stream):
         ws = mb.Workspace(T, K, E, device=dev, stream=stream)
         bufs = mb.pack(emb, asgn, wts, E, workspace=ws, stream=stream)
         out = torch.empty((T, d), dtype=tdtype, device=dev)
-
+        if layer:
+            I = c["I"]
+            # random-init experts ~N(0, 0.02), seeded by GLOBAL expert id so every
+            # rank count uses the same weights (apps/bench_prefill.cu:432-439)
+            wgu = torch.empty((hi - lo, 2 * I, d), dtype=tdtype, device=dev)
+            wdn = torch.empty((hi - lo, d, I), dtype=tdtype, device=dev)
+            for j, e in enumerate(range(lo, hi)):
+                g = torch.Generator(device=dev)
+                g.manual_seed(1000 + e)
+                wgu[j] = (torch.randn((2 * I, d), generator=g, device=dev) * 0.02).to(tdtype)
+                wdn[j] = (torch.randn((d, I), generator=g, device=dev) * 0.02).to(tdtype)
+            cap = world * TK if world > 1 else TK
+            h_buf = torch.empty((cap, I), dtype=tdtype, device=dev)
+            y_buf = torch.empty((cap, d), dtype=tdtype, device=dev)
     if world > 1:
-        import ep
-        bounds = ep.expert_ranges(E, world)
-        bounds_dev = torch.tensor(bounds, dtype=torch.long, device=dev)
+        epx = ep.ExpertParallel(E, device=dev)
         recv_buf = torch.empty((world * TK, d), dtype=tdtype, device=dev)
         back_buf = torch.empty((TK, d), dtype=tdtype, device=dev)
 
     def step(split=False):
-        """One pass.  Returns CUDA events recorded on the launching stream at the
-        step boundaries, plus one between pack and the rest when `split` (an
-        event there costs the PDL overlap, so the headline loop omits it)."""
-        evs = [torch.cuda.Event(enable_timing=True) for _ in range(3 if split else 2)]
+        """One pass.  Returns CUDA events recorded on the launching stream: the
+        step boundaries only, or with `split` six boundaries [start, pack done,
+        expert start, expert done, combine done, end] (an event between
+        kernels costs the PDL overlap, so the headline loop does not split)."""
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(6 if split else 2)]
+        mark = (lambda i: evs[i].record(stream)) if split else (lambda i: None)
         evs[0].record(stream)
         mb.pack(emb, asgn, wts, E, workspace=ws, out=bufs, stream=stream)
-        if split:
-            evs[1].record(stream)
-        y = bufs.packed
+        mark(1)
         if world > 1:
-            starts = bufs.expert_start.long()
-            send = (starts[bounds_dev[1:]] - starts[bounds_dev[:-1]]).to(torch.int64)
-            recv = torch.empty_like(send)
-            dist.all_to_all_single(recv, send)
-            counts = torch.stack([send, recv]).cpu()  # host split sizes (one D2H, as the reference)
-            s_list, r_list = counts[0].tolist(), counts[1].tolist()
-            nrecv = sum(r_list)
-            dist.all_to_all_single(recv_buf[:nrecv], bufs.packed, r_list, s_list)
-            # identity expert on recv_buf[:nrecv]; combine back to the senders' packed order
-            dist.all_to_all_single(back_buf, recv_buf[:nrecv], s_list, r_list)
-            y = back_buf
+            x_in, lay = epx.dispatch(bufs.packed, bufs.expert_count, recv_buf)
+            seg_start, seg_expert = lay.seg_start, lay.seg_expert
+        else:
+            x_in, seg_start, seg_expert = bufs.packed, bufs.expert_start, None
+        mark(2)
+        if layer:
+            n = x_in.shape[0]
+            _, y = mb.grouped_swiglu(x_in, seg_start, wgu, wdn, seg_expert=seg_expert,
+                                     h=h_buf[:n], y=y_buf[:n], stream=stream)
+        else:
+            y = x_in                                  # identity expert
+        mark(3)
+        if world > 1:
+            y = epx.combine(y, lay, back_buf)
+        mark(4)
         mb.unpermute(y, bufs.packed_weights, bufs.slot_pos, T, K, out=out, stream=stream)
         evs[-1].record(stream)
         return evs
@@ -361,9 +396,13 @@ def gpu_arm(args):
             step()
         torch.cuda.synchronize(dev)
         assert ws.device_status(stream) == 0, "device-side condition during warm-up"
-        # correctness gate before timing (identity expert closed form)
-        ref = (wts.sum(dim=1, keepdim=True) * emb.float())
-        torch.testing.assert_close(out.float(), ref, rtol=1e-3, atol=1e-3)
+        assert mb.device_status(stream) == 0, "device-side condition during warm-up"
+        if not layer:
+            # correctness gate before timing (identity expert closed form)
+            ref = (wts.sum(dim=1, keepdim=True) * emb.float())
+            torch.testing.assert_close(out.float(), ref, rtol=1e-3, atol=1e-3)
+        else:
+            assert bool(torch.isfinite(out.float()).all()), "non-finite layer output"
 
         if world > 1:
             dist.barrier()
@@ -377,7 +416,7 @@ def gpu_arm(args):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
-        # attribution loop: the same steps with an event between pack and the rest
+        # attribution loop: the same steps with events between the stages
         split = []
         for i in range(args.steps):
             flusher(i)
@@ -387,58 +426,91 @@ def gpu_arm(args):
             dist.barrier()
 
     step_ms = [a.elapsed_time(b) for a, b in rec]
-    pack_ms = [a.elapsed_time(b) for a, b, _ in split]
-    rest_ms = [b.elapsed_time(cc) for _, b, cc in split]
+    pack_ms = [e[0].elapsed_time(e[1]) for e in split]
+    mid_ms = [e[1].elapsed_time(e[4]) for e in split]       # dispatch + expert + combine
+    expert_ms = [e[2].elapsed_time(e[3]) for e in split]
+    unperm_ms = [e[4].elapsed_time(e[5]) for e in split]
     total_ms = sum(step_ms)
+    stage = torch.tensor([statistics.fmean(pack_ms), statistics.fmean(mid_ms), statistics.fmean(expert_ms),
+                          statistics.fmean(unperm_ms)], dtype=torch.float64, device=dev)
     if world > 1:
         t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
+        dist.all_reduce(stage, op=dist.ReduceOp.MAX)
+    mean_pack, mean_mid, mean_expert, mean_unperm = stage.tolist()
 
-    # e2e through the C ABI with pinned host buffers (N = 1 only)
+    # e2e through the C ABI with pinned host buffers (N = 1, identity expert)
     e2e = None
-    if world == 1 and not args.no_e2e:
+    if world == 1 and not args.no_e2e and not layer:
         e2e = e2e_leg(mb, c, emb, asgn_np, wts_np, ws, stream, dev, args.steps, warm)
 
     if rank == 0:
-        b_pack, b_unperm = algorithmic_bytes(c)
         ms = total_ms / args.steps
-        value = world * T * args.steps / (total_ms / 1e3)
-        mean_pack = statistics.fmean(pack_ms)
-        mean_rest = statistics.fmean(rest_ms)
-        peak, peak_src = measured_peaks()
-        if mean_rest >= mean_pack or world > 1:
-            dom, dom_bytes, dom_ms = "unpermute_bulk_kernel", b_unperm, mean_rest
-        else:
-            dom, dom_bytes, dom_ms = "pack (route_scan_kernel + pack_rows_bulk_kernel)", b_pack, mean_pack
-        if world > 1:
-            dom, dom_bytes, dom_ms = "pack (route_scan_kernel + pack_rows_bulk_kernel)", b_pack, mean_pack
-        achieved = dom_bytes / (dom_ms / 1e3) / 1e9
-        traffic_key = "unpermute_kernel" if dom.startswith("unpermute") else "pack"
+        b_pack, b_unperm = algorithmic_bytes(c)
+        peak_hbm, src_hbm = measured_peaks()
+        kernels = ["route_scan_kernel", "pack_rows_bulk_kernel", "unpermute_bulk_kernel"]
+        if layer:
+            kernels[2:2] = ["grouped_gemm_kernel<SwiGLU>", "grouped_gemm_kernel<store>"]
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "fp16 rows (bitwise pack), fp32 combine accumulate",
-            "data": "synthetic (seeded Gumbel top-K routing, N(0,1) rows)",
+            "metric": METRIC_LAYER if layer else METRIC,
+            "unit": "us" if layer else UNIT,
+            "value": ms * 1e3 if layer else world * T * args.steps / (total_ms / 1e3),
+            "n_gpus": world, "steps": args.steps, "warmup": warm, "ms_per_step": ms,
+            "higher_is_better": not layer, "scaling": "strong" if layer else "weak",
+            "vs_baseline": None,
+            "dtype": ("bf16 rows and weights, fp32 accumulate" if layer
+                      else "fp16 rows (bitwise pack), fp32 combine accumulate"),
+            "data": "synthetic (seeded Gumbel top-K routing, N(0,1) rows" +
+                    (", N(0,0.02) random-init experts)" if layer else ")"),
             "config": config_json(c, world, L2_NOTE),
-            "hbm_gbs": (b_pack + b_unperm) / (ms / 1e3) / 1e9 if world == 1 else None,
-            "stages_ms": {"pack": mean_pack, "unpermute" if world == 1 else "dispatch+combine+unpermute": mean_rest,
-                          "note": "separate loop with an extra event between the stages (costs the "
-                                  "PDL overlap); the headline step has events at its boundaries only"},
-            "roofline": {
-                "bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"
-                if peak_src == "measured" else "fallback 6.65 TB/s",
-                "algorithmic_bytes_per_launch": dom_bytes,
-                "traffic": committed_traffic(traffic_key, c["name"]),
-            },
-            "gpu_launches": 3 * args.steps,
-            "kernels_per_step": ["route_scan_kernel", "pack_rows_bulk_kernel", "unpermute_bulk_kernel"],
+            "stages_ms": {"pack": mean_pack,
+                          ("dispatch+ffn+combine" if world > 1 else "ffn") if layer else
+                          ("dispatch+combine" if world > 1 else "identity"): mean_mid,
+                          "unpermute": mean_unperm,
+                          "note": "max over ranks of the per-rank means, from a separate loop with events "
+                                  "between the stages (costs the PDL overlap); the headline step has events "
+                                  "at its boundaries only"},
+            "gpu_launches": len(kernels) * args.steps + (args.steps if world > 1 else 0),
+            "kernels_per_step": kernels + (["ep_layout_kernel"] if world > 1 else []),
             "clocks": clk.summary(),
         }
+        if layer:
+            I = c["I"]
+            flops = 6 * world * TK * d * I  # all ranks' FFN work; per rank ~ 6 * TK * d * I
+            tf_peak, tf_src = measured_tflops()
+            achieved = 6 * TK * d * I / (mean_expert / 1e3) / 1e12
+            line["tokens_per_s"] = world * T * args.steps / (total_ms / 1e3)
+            line["roofline"] = {
+                "bound": "tensor", "kernel": "grouped_gemm_kernel (SwiGLU GEMM + down GEMM)",
+                "achieved": achieved, "peak": tf_peak, "unit": "TFLOP/s", "frac": achieved / tf_peak,
+                "peak_source": tf_src, "algorithmic_flops_per_launch": 6 * TK * d * I,
+                "traffic": committed_traffic("grouped_ffn", c["name"]),
+            }
+            line["ffn_ms"] = mean_expert
+        else:
+            if world == 1:
+                line["hbm_gbs"] = (b_pack + b_unperm) / (ms / 1e3) / 1e9
+            if mean_unperm >= mean_pack and world == 1:
+                dom, dom_bytes, dom_ms, key = "unpermute_bulk_kernel", b_unperm, mean_unperm, "unpermute_kernel"
+            else:
+                dom, dom_bytes, dom_ms, key = ("pack (route_scan_kernel + pack_rows_bulk_kernel)", b_pack,
+                                               mean_pack, "pack")
+            achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+            line["roofline"] = {
+                "bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak_hbm, "unit": "GB/s",
+                "frac": achieved / peak_hbm,
+                "peak_source": (f"{src_hbm} (MEASURED_PEAKS.json hbm_gbs)" if src_hbm == "measured"
+                                else "fallback 6.65 TB/s"),
+                "algorithmic_bytes_per_launch": dom_bytes,
+                "traffic": committed_traffic(key, c["name"]),
+            }
+        if world > 1:
+            line["ep"] = {"experts_per_rank": [bounds[g + 1] - bounds[g] for g in range(world)],
+                          "collectives": "NCCL all_gather (counts) + 2 x all_to_all_single (rows)"}
         if e2e is not None:
             line["e2e"] = e2e
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and not layer:
             cv, per, kind = run_cpu(c, 1, c["T"], 5, 1, min_seconds=10.0)
             line["cpu_baseline"] = {
                 "value": cv, "unit": UNIT, "cores": 1, "kind": kind,

@@ -152,7 +152,7 @@ int moe_b200_unpermute(const void* y, const float* packed_weights, const int32_t
  *   w_down     [E, d, I]       row c: output column c over the I inner features
  *   h          [rows, I]       out: the SwiGLU intermediate
  *   y          [rows, d]       out: expert outputs, in packed order
- * d and I multiples of 16; all pointers 16-byte aligned; nseg <= 4096.
+ * d and I multiples of 16; all pointers 16-byte aligned; nseg <= 2048.
  * Replaces the per-expert cublasHgemm loop (apps/bench_e2e.cu:274-301,
  * apps/bench_prefill.cu:854-884) and the CUTLASS sm80 GemmGrouped FFN
  * (apps/bench_prefill.cu:68-202, 812-852), which have no activation and need
@@ -162,6 +162,27 @@ int moe_b200_grouped_swiglu(const void* x, const int32_t* seg_start, const int32
                             int nseg, int rows, int d, int I, int E,
                             const void* w_gate_up, const void* w_down, int dtype,
                             void* h, void* y, void* stream);
+
+/* ----------------------------------------------------- expert parallel ---- */
+
+/* Exchange layout of rank `rank` among `nranks` expert-parallel ranks, on the
+ * device.  Experts are owned in contiguous ranges: rank g owns
+ * [expert_first[g], expert_first[g+1]) (host array, nranks+1 entries, may be
+ * uneven).  all_counts [nranks, E]: every rank's expert_count (one all-gather).
+ *   send_counts [nranks]  rows of this rank's packed buffer for rank g -- the
+ *                         packed buffer is already the rank-major send buffer
+ *   recv_counts [nranks]  rows received from rank g
+ *   seg_start   [nranks*L + 1], seg_expert [nranks*L]  (L = local experts):
+ *                         the receive buffer's segments, sender-major then
+ *                         local-expert-major; seg_expert is the local expert
+ *                         index, as moe_b200_grouped_swiglu expects.
+ * Replaces the host-side offset computation after a D2H copy
+ * (apps/bench_prefill.cu:768-788) and the per-round host FFN problem list
+ * (apps/bench_prefill.cu:812-852).  nranks <= 64.                          */
+int moe_b200_ep_layout(const int32_t* all_counts, int nranks, int E, int rank,
+                       const int32_t* expert_first /* host */, int32_t* seg_start,
+                       int32_t* seg_expert, int32_t* send_counts, int32_t* recv_counts,
+                       void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */
