@@ -181,6 +181,16 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 uint32_t* device_status_word();  // status.cu
 
+// After the route/scan grid has finished (PDL wait done): re-zero its ticket
+// and look-back words so the workspace is ready for the next call.
+__device__ __forceinline__ void rearm_scan_scratch(WsHeader* hdr, uint64_t* status, size_t words) {
+    const size_t gt = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t nt = size_t(gridDim.x) * blockDim.x;
+    for (size_t i = gt; i < words; i += nt) status[i] = 0;
+    if (gt == 0) hdr->ticket = 0;
+}
+
+
 // Launch configuration that lets the kernel start while the previous kernel
 // in the stream finishes (programmatic dependent launch); the kernel must call
 // pdl_wait_primary() before touching anything the previous kernel writes.

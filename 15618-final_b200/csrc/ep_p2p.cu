@@ -1,0 +1,552 @@
+// ep_p2p.cu -- fused expert-parallel dispatch and combine over peer memory
+// (NVLink / NVSwitch), one process per GPU.
+//
+// Each rank owns one symmetric region (one cudaMalloc, the same layout on
+// every rank) that its peers map through CUDA IPC:
+//   [counts flags | data flags | back flags]  one u64 epoch word per sender
+//   inbox  [N][E] int32        every rank's expert counts for this step
+//   recv   [N * max_tokens * K][d]   rows routed to this rank's experts,
+//                              sender-major then local-expert-major
+//   back   [max_tokens * K][d] this rank's rows after their expert, in its
+//                              own packed order
+// One step (epoch e, the same on all ranks; epochs only grow, so no word is
+// ever reset):
+//   1. route_scan (pack.cu) -> local counts / starts / ranks
+//   2. ep_publish_kernel: write the counts into every peer's inbox, raise
+//      counts flag = e on every peer (system-scope release)
+//   3. ep_pack_dispatch_kernel: wait for all counts, then every token row is
+//      read once and stored K times straight into the receive buffer of the
+//      rank owning each slot's expert (NVLink stores); the last CTA raises
+//      data flag = e on every peer
+//   4. ep_receive_kernel (receiver): wait for all data flags, build the
+//      segment table of the receive buffer + each segment's return address
+//   5. the expert: grouped SwiGLU whose down-GEMM epilogue stores every row
+//      straight into the sender's back buffer (grouped_ffn.cu scatter mode),
+//      or ep_return_identity_kernel; then ep_signal_kernel raises back flags
+//   6. ep_wait_kernel (sender) waits for all back flags; unpermute reads the
+//      local back buffer
+// The host never waits inside a step.  This replaces the reference's
+// AllGather -> D2H -> host offsets -> grouped ncclSend/ncclRecv exchange
+// (apps/bench_prefill.cu:768-807, 889-906).  Every wait is bounded (the
+// context's timeout); on expiry the kernel sets MOE_B200_DEV_WAIT_TIMEOUT in
+// the library's device status word and carries on.  Only plain loads and
+// stores touch peer memory (no TMA, no multicast).
+#include <cstring>
+#include <mutex>
+
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace moe_b200 {
+
+int fail(int code, const char* fmt, ...);
+int cuda_fail(cudaError_t err, const char* where);
+cudaError_t launch_route_scan(const int32_t* asgn, int T, int K, int E, int32_t* expert_count,
+                              int32_t* expert_start, void* ws, cudaStream_t stream);
+cudaError_t launch_unpermute(const void* y, const float* packed_w, const int32_t* slot_pos, int T, int K,
+                             int d, int dtype, void* out, cudaStream_t stream);
+int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* seg_expert, int nseg, int rows,
+                        int d, int I, int E, const void* w_gate_up, const void* w_down, int dtype, void* h,
+                        void* y, cudaStream_t s, char* const* dst_base, const int32_t* seg_src,
+                        const int32_t* seg_dst_row);
+
+constexpr int kEpMaxRanks = 64;
+
+struct EpGeom {
+    int nranks, rank, E, K, d, max_tokens;
+    int first[kEpMaxRanks + 1];
+    size_t off_cflag, off_dflag, off_bflag, off_inbox, off_recv, off_back, total;
+    int64_t recv_cap;
+    uint64_t timeout_ns;
+};
+
+struct EpContext {
+    EpGeom g;
+    int device = -1;
+    char* region = nullptr;
+    char* peer_host[kEpMaxRanks] = {};
+    bool opened[kEpMaxRanks] = {};
+    char** peer_dev = nullptr;   // device array: every rank's region in this address space
+    char** back_dev = nullptr;   // device array: every rank's back buffer
+    bool connected = false;
+};
+
+static size_t al4k(size_t x) { return (x + 4095) & ~size_t(4095); }
+
+// ---------------------------------------------------------------- device ----
+
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Bounded wait until flags[i] >= epoch for i in [0, n), one thread per flag.
+// Returns false (and records a timeout) if any flag did not arrive in time.
+__device__ bool wait_flags(const uint64_t* flags, int n, uint64_t epoch, uint64_t timeout_ns,
+                           uint32_t* dev_status, int* s_fail) {
+    if (threadIdx.x < n) {
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire_sys(flags + threadIdx.x) < epoch) {
+            if (globaltimer_ns() - t0 > timeout_ns) {
+                atomicOr(dev_status, MOE_B200_DEV_WAIT_TIMEOUT);
+                *s_fail = 1;
+                break;
+            }
+            __nanosleep(100);
+        }
+    }
+    __syncthreads();
+    return *s_fail == 0;
+}
+
+__global__ void __launch_bounds__(256)
+ep_publish_kernel(EpGeom g, char* const* __restrict__ peer, const int32_t* __restrict__ expert_count,
+                  uint64_t epoch) {
+    for (int p = 0; p < g.nranks; ++p) {
+        int32_t* dst = reinterpret_cast<int32_t*>(peer[p] + g.off_inbox) + size_t(g.rank) * g.E;
+        for (int e = threadIdx.x; e < g.E; e += blockDim.x) dst[e] = expert_count[e];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < g.nranks)
+        st_release_sys(reinterpret_cast<uint64_t*>(peer[threadIdx.x] + g.off_cflag) + g.rank, epoch);
+}
+
+// Warp per token: row read once (16-byte loads), stored to the receive buffer
+// of the rank owning each slot's expert.
+__global__ void __launch_bounds__(256)
+ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* __restrict__ emb,
+                        const int32_t* __restrict__ asgn, const float* __restrict__ wts,
+                        const int32_t* __restrict__ rank, const int32_t* __restrict__ expert_start, int T,
+                        float* __restrict__ packed_w, int32_t* __restrict__ perm,
+                        int32_t* __restrict__ slot_pos, WsHeader* __restrict__ hdr,
+                        uint64_t* __restrict__ status, size_t status_words, uint64_t epoch,
+                        uint32_t* __restrict__ dev_status) {
+    __shared__ int64_t dst_off[kEpMaxRanks];  // receive row of packed position p on rank r = dst_off[r] + p
+    __shared__ int s_fail;
+    extern __shared__ int32_t s_owner[];      // [E]
+    const int K = g.K, nvec = g.d / 8;
+    if (threadIdx.x == 0) s_fail = 0;
+    __syncthreads();
+    pdl_wait_primary();
+    rearm_scan_scratch(hdr, status, status_words);
+    const char* mine = peer[g.rank];
+    wait_flags(reinterpret_cast<const uint64_t*>(mine + g.off_cflag), g.nranks, epoch, g.timeout_ns, dev_status,
+               &s_fail);
+    const int32_t* inbox = reinterpret_cast<const int32_t*>(mine + g.off_inbox);
+    for (int e = threadIdx.x; e < g.E; e += blockDim.x) {
+        int r = 0;
+        while (r + 1 < g.nranks && g.first[r + 1] <= e) ++r;
+        s_owner[e] = r;
+    }
+    if (threadIdx.x < g.nranks) {
+        const int r = threadIdx.x;
+        int64_t base = 0;
+        for (int s = 0; s < g.rank; ++s)
+            for (int e = g.first[r]; e < g.first[r + 1]; ++e) base += inbox[s * g.E + e];
+        dst_off[r] = base - expert_start[g.first[r]];
+    }
+    __syncthreads();
+
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t nw = int64_t(gridDim.x) * (blockDim.x >> 5);
+    const size_t rowb = size_t(g.d) * 2;
+    constexpr int VPL = 8;
+    for (int64_t t = gw; t < T && !s_fail; t += nw) {
+        uint4* dst_lane = nullptr;
+        if (lane < K) {
+            const int64_t sidx = t * K + lane;
+            const int32_t r = rank[sidx];
+            int32_t p = -1;
+            if (r >= 0) {
+                const int e = __ldg(asgn + sidx);
+                p = expert_start[e] + r;
+                perm[p] = int32_t(t);
+                if (packed_w) packed_w[p] = __ldg(wts + sidx);
+                const int owner = s_owner[e];
+                dst_lane = reinterpret_cast<uint4*>(peer[owner] + g.off_recv + size_t(dst_off[owner] + p) * rowb);
+            }
+            if (slot_pos) slot_pos[sidx] = p;
+        }
+        const uint4* src = emb + t * nvec;
+        for (int c0 = 0; c0 < nvec; c0 += 32 * VPL) {
+            uint4 v[VPL];
+#pragma unroll
+            for (int j = 0; j < VPL; ++j) {
+                const int i = c0 + j * 32 + lane;
+                v[j] = i < nvec ? ld_nc_v4(src + i) : make_uint4(0, 0, 0, 0);
+            }
+            for (int k = 0; k < K; ++k) {
+                uint4* dst = reinterpret_cast<uint4*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(dst_lane), k));
+                if (!dst) continue;
+#pragma unroll
+                for (int j = 0; j < VPL; ++j) {
+                    const int i = c0 + j * 32 + lane;
+                    if (i < nvec) st_v4(dst + i, v[j]);
+                }
+            }
+        }
+    }
+    // The last CTA to finish announces the rows to every receiver.
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t prev = atomicAdd(&hdr->pad[0], 1u);
+        if (prev == gridDim.x - 1) {
+            hdr->pad[0] = 0;
+            __threadfence_system();
+            for (int p = 0; p < g.nranks; ++p)
+                st_release_sys(reinterpret_cast<uint64_t*>(peer[p] + g.off_dflag) + g.rank, epoch);
+        }
+    }
+}
+
+// Receiver: wait for every sender's rows, then the segment table of the
+// receive buffer with the return address of each segment.
+__global__ void __launch_bounds__(256)
+ep_receive_kernel(EpGeom g, char* const* __restrict__ peer, uint64_t epoch, int32_t* __restrict__ seg_start,
+                  int32_t* __restrict__ seg_expert, int32_t* __restrict__ seg_src,
+                  int32_t* __restrict__ seg_dst_row, uint32_t* __restrict__ dev_status) {
+    __shared__ int s_fail;
+    __shared__ int32_t warp_tot[8];
+    __shared__ int32_t carry;
+    if (threadIdx.x == 0) {
+        s_fail = 0;
+        carry = 0;
+    }
+    __syncthreads();
+    const char* mine = peer[g.rank];
+    wait_flags(reinterpret_cast<const uint64_t*>(mine + g.off_dflag), g.nranks, epoch, g.timeout_ns, dev_status,
+               &s_fail);
+    const int32_t* inbox = reinterpret_cast<const int32_t*>(mine + g.off_inbox);
+    const int lo = g.first[g.rank], L = g.first[g.rank + 1] - lo;
+    const int nseg = g.nranks * L;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int base = 0; base < nseg; base += blockDim.x) {
+        const int i = base + tid;
+        int32_t v = 0;
+        if (i < nseg) {
+            const int s = i / L, j = i % L;
+            v = inbox[s * g.E + lo + j];
+            seg_expert[i] = j;
+            seg_src[i] = s;
+            int32_t before = 0;  // sender s's packed start of expert lo + j
+            for (int e = 0; e < lo + j; ++e) before += inbox[s * g.E + e];
+            seg_dst_row[i] = before;
+        }
+        int32_t incl = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += n;
+        }
+        if (lane == 31) warp_tot[warp] = incl;
+        __syncthreads();
+        int32_t off = carry;
+        for (int w = 0; w < warp; ++w) off += warp_tot[w];
+        if (i < nseg) seg_start[i] = off + incl - v;
+        __syncthreads();
+        if (tid == blockDim.x - 1) carry = off + incl;
+        __syncthreads();
+    }
+    if (tid == 0) seg_start[nseg] = carry;
+}
+
+// Identity expert: every received row goes back to its sender's back buffer.
+__global__ void __launch_bounds__(256)
+ep_return_identity_kernel(EpGeom g, char* const* __restrict__ back, const uint4* __restrict__ recv,
+                          const int32_t* __restrict__ seg_start, const int32_t* __restrict__ seg_src,
+                          const int32_t* __restrict__ seg_dst_row, int nseg) {
+    pdl_wait_primary();
+    const int nvec = g.d / 8;
+    const int lane = threadIdx.x & 31;
+    const int64_t total = seg_start[nseg];
+    const int64_t gw = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t nw = int64_t(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t row = gw; row < total; row += nw) {
+        int lo = 0, hi = nseg - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (seg_start[mid] <= row) lo = mid;
+            else hi = mid - 1;
+        }
+        const int64_t drow = int64_t(seg_dst_row[lo]) + (row - seg_start[lo]);
+        uint4* dst = reinterpret_cast<uint4*>(back[seg_src[lo]]) + drow * nvec;
+        const uint4* src = recv + row * nvec;
+        for (int i = lane; i < nvec; i += 32) st_v4(dst + i, ld_nc_v4(src + i));
+    }
+    __threadfence_system();
+}
+
+// Raise flag word `flag_off`[rank] = epoch on every rank (after all prior
+// work of this stream, whose peer stores were fenced system-wide).
+__global__ void ep_signal_kernel(EpGeom g, char* const* __restrict__ peer, size_t flag_off, uint64_t epoch) {
+    pdl_wait_primary();
+    __threadfence_system();
+    if (threadIdx.x < g.nranks)
+        st_release_sys(reinterpret_cast<uint64_t*>(peer[threadIdx.x] + flag_off) + g.rank, epoch);
+}
+
+__global__ void ep_wait_kernel(EpGeom g, const char* __restrict__ mine, size_t flag_off, uint64_t epoch,
+                               uint32_t* __restrict__ dev_status) {
+    __shared__ int s_fail;
+    if (threadIdx.x == 0) s_fail = 0;
+    __syncthreads();
+    wait_flags(reinterpret_cast<const uint64_t*>(mine + flag_off), g.nranks, epoch, g.timeout_ns, dev_status,
+               &s_fail);
+    __threadfence_system();
+}
+
+// ------------------------------------------------------------------ host ----
+
+static int sm_count_ep() {
+    int dev = 0, n = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+static EpContext* as_ctx(void* c) {
+    EpContext* ctx = static_cast<EpContext*>(c);
+    return ctx;
+}
+
+}  // namespace moe_b200
+
+using namespace moe_b200;
+
+extern "C" {
+
+int moe_b200_ep_create(int nranks, int rank, int E, int K, int d, int max_tokens, const int32_t* expert_first,
+                       int timeout_ms, void** ctx_out) {
+    if (!ctx_out || !expert_first) return fail(MOE_B200_ERR_INVALID_ARG, "ep_create: null pointer");
+    if (nranks < 1 || nranks > kEpMaxRanks || rank < 0 || rank >= nranks || E < nranks || K < 1 || K > 32 ||
+        d < 8 || d % 8 != 0 || max_tokens < 1 || timeout_ms < 1)
+        return fail(MOE_B200_ERR_INVALID_ARG,
+                    "ep_create: need 1<=nranks<=%d, 0<=rank<nranks, E>=nranks, 1<=K<=32, d%%8==0, "
+                    "max_tokens>=1, timeout_ms>=1",
+                    kEpMaxRanks);
+    if (expert_first[0] != 0 || expert_first[nranks] != E)
+        return fail(MOE_B200_ERR_INVALID_ARG, "ep_create: expert_first must run from 0 to E");
+    EpContext* ctx = new EpContext();
+    EpGeom& g = ctx->g;
+    g.nranks = nranks;
+    g.rank = rank;
+    g.E = E;
+    g.K = K;
+    g.d = d;
+    g.max_tokens = max_tokens;
+    for (int i = 0; i <= nranks; ++i) {
+        g.first[i] = expert_first[i];
+        if (i > 0 && expert_first[i] <= expert_first[i - 1]) {
+            delete ctx;
+            return fail(MOE_B200_ERR_INVALID_ARG, "ep_create: every rank must own at least one expert");
+        }
+    }
+    g.off_cflag = 0;
+    g.off_dflag = 8 * kEpMaxRanks;
+    g.off_bflag = 16 * kEpMaxRanks;
+    g.off_inbox = 4096;
+    g.off_recv = g.off_inbox + al4k(size_t(nranks) * E * 4);
+    g.recv_cap = int64_t(nranks) * max_tokens * K;
+    g.off_back = g.off_recv + al4k(size_t(g.recv_cap) * d * 2);
+    g.total = g.off_back + al4k(size_t(max_tokens) * K * d * 2);
+    g.timeout_ns = uint64_t(timeout_ms) * 1000000ull;
+    cudaError_t err = cudaGetDevice(&ctx->device);
+    if (err == cudaSuccess) err = cudaMalloc(&ctx->region, g.total);
+    if (err == cudaSuccess) err = cudaMemset(ctx->region, 0, g.total);
+    if (err == cudaSuccess) err = cudaMalloc(&ctx->peer_dev, sizeof(char*) * kEpMaxRanks * 2);
+    if (err != cudaSuccess) {
+        if (ctx->region) cudaFree(ctx->region);
+        delete ctx;
+        return cuda_fail(err, "ep_create");
+    }
+    ctx->back_dev = ctx->peer_dev + kEpMaxRanks;
+    *ctx_out = ctx;
+    return MOE_B200_OK;
+}
+
+int moe_b200_ep_destroy(void* c) {
+    EpContext* ctx = as_ctx(c);
+    if (!ctx) return MOE_B200_OK;
+    cudaDeviceSynchronize();
+    for (int p = 0; p < ctx->g.nranks; ++p)
+        if (ctx->opened[p]) cudaIpcCloseMemHandle(ctx->peer_host[p]);
+    if (ctx->peer_dev) cudaFree(ctx->peer_dev);
+    if (ctx->region) cudaFree(ctx->region);
+    delete ctx;
+    return MOE_B200_OK;
+}
+
+int moe_b200_ep_ipc_handle(void* c, void* handle_out) {
+    EpContext* ctx = as_ctx(c);
+    if (!ctx || !handle_out) return fail(MOE_B200_ERR_INVALID_ARG, "ep_ipc_handle: null pointer");
+    cudaIpcMemHandle_t h;
+    cudaError_t err = cudaIpcGetMemHandle(&h, ctx->region);
+    if (err != cudaSuccess) return cuda_fail(err, "ep_ipc_handle");
+    std::memcpy(handle_out, &h, sizeof(h));
+    return MOE_B200_OK;
+}
+
+int moe_b200_ep_connect(void* c, const void* handles) {
+    EpContext* ctx = as_ctx(c);
+    if (!ctx || !handles) return fail(MOE_B200_ERR_INVALID_ARG, "ep_connect: null pointer");
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handles are 64 bytes");
+    const EpGeom& g = ctx->g;
+    char* back[kEpMaxRanks];
+    for (int p = 0; p < g.nranks; ++p) {
+        if (p == g.rank) {
+            ctx->peer_host[p] = ctx->region;
+        } else if (!ctx->opened[p]) {
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, static_cast<const char*>(handles) + 64 * p, 64);
+            void* ptr = nullptr;
+            cudaError_t err = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+            if (err != cudaSuccess) return cuda_fail(err, "ep_connect: cudaIpcOpenMemHandle");
+            ctx->peer_host[p] = static_cast<char*>(ptr);
+            ctx->opened[p] = true;
+        }
+        back[p] = ctx->peer_host[p] + g.off_back;
+    }
+    cudaError_t err = cudaMemcpy(ctx->peer_dev, ctx->peer_host, sizeof(char*) * g.nranks, cudaMemcpyHostToDevice);
+    if (err == cudaSuccess) err = cudaMemcpy(ctx->back_dev, back, sizeof(char*) * g.nranks, cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) return cuda_fail(err, "ep_connect");
+    ctx->connected = true;
+    return MOE_B200_OK;
+}
+
+void* moe_b200_ep_recv_rows(void* c) {
+    EpContext* ctx = as_ctx(c);
+    return ctx ? ctx->region + ctx->g.off_recv : nullptr;
+}
+
+void* moe_b200_ep_back_rows(void* c) {
+    EpContext* ctx = as_ctx(c);
+    return ctx ? ctx->region + ctx->g.off_back : nullptr;
+}
+
+int64_t moe_b200_ep_recv_capacity(void* c) {
+    EpContext* ctx = as_ctx(c);
+    return ctx ? ctx->g.recv_cap : 0;
+}
+
+int moe_b200_ep_dispatch(void* c, uint64_t epoch, const void* emb, const int32_t* asgn, const float* wts, int T,
+                         float* packed_weights, int32_t* perm, int32_t* expert_count, int32_t* expert_start,
+                         int32_t* slot_pos, void* workspace, size_t workspace_bytes, void* stream) {
+    EpContext* ctx = as_ctx(c);
+    if (!ctx || !ctx->connected) return fail(MOE_B200_ERR_INVALID_ARG, "ep_dispatch: context not connected");
+    const EpGeom& g = ctx->g;
+    if (T < 1 || T > g.max_tokens || !emb || !asgn || !perm || !expert_count || !expert_start || !slot_pos ||
+        (packed_weights && !wts))
+        return fail(MOE_B200_ERR_INVALID_ARG, "ep_dispatch: need 1 <= T <= max_tokens and all buffers");
+    if (reinterpret_cast<uintptr_t>(emb) % 16 != 0)
+        return fail(MOE_B200_ERR_INVALID_ARG, "ep_dispatch: rows must be 16-byte aligned");
+    const PackPlan plan = plan_pack(T, g.K, g.E);
+    if (!workspace || workspace_bytes < plan.total_bytes || reinterpret_cast<uintptr_t>(workspace) % 256)
+        return fail(MOE_B200_ERR_WORKSPACE, "ep_dispatch: workspace of %zu bytes (256-aligned) needed",
+                    plan.total_bytes);
+    uint32_t* st = device_status_word();
+    if (!st) return fail(MOE_B200_ERR_CUDA, "ep_dispatch: device status word unavailable");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t err = launch_route_scan(asgn, T, g.K, g.E, expert_count, expert_start, workspace, s);
+    if (err == cudaSuccess) {
+        ep_publish_kernel<<<1, 256, 0, s>>>(g, ctx->peer_dev, expert_count, epoch);
+        err = cudaGetLastError();
+    }
+    if (err == cudaSuccess) {
+        char* base = static_cast<char*>(workspace);
+        int grid = sm_count_ep() * 4;
+        const int want = (T + 7) / 8;
+        if (grid > want) grid = want;
+        cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(256), size_t(g.E) * 4, s);
+        cudaLaunchAttribute attr = pdl_attr();
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        err = cudaLaunchKernelEx(&cfg, ep_pack_dispatch_kernel, g, static_cast<char* const*>(ctx->peer_dev),
+                                 static_cast<const uint4*>(emb), asgn, wts,
+                                 static_cast<const int32_t*>(reinterpret_cast<int32_t*>(base + plan.rank_off)),
+                                 static_cast<const int32_t*>(expert_start), T, packed_weights, perm, slot_pos,
+                                 reinterpret_cast<WsHeader*>(base),
+                                 reinterpret_cast<uint64_t*>(base + plan.status_off),
+                                 size_t(plan.num_tiles) * size_t(g.E), epoch, st);
+    }
+    return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "ep_dispatch launch");
+}
+
+int moe_b200_ep_receive(void* c, uint64_t epoch, int32_t* seg_start, int32_t* seg_expert, int32_t* seg_src,
+                        int32_t* seg_dst_row, void* stream) {
+    EpContext* ctx = as_ctx(c);
+    if (!ctx || !ctx->connected) return fail(MOE_B200_ERR_INVALID_ARG, "ep_receive: context not connected");
+    if (!seg_start || !seg_expert || !seg_src || !seg_dst_row)
+        return fail(MOE_B200_ERR_INVALID_ARG, "ep_receive: null segment buffer");
+    uint32_t* st = device_status_word();
+    if (!st) return fail(MOE_B200_ERR_CUDA, "ep_receive: device status word unavailable");
+    ep_receive_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        ctx->g, ctx->peer_dev, epoch, seg_start, seg_expert, seg_src, seg_dst_row, st);
+    cudaError_t err = cudaGetLastError();
+    return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "ep_receive launch");
+}
+
+int moe_b200_ep_return_identity(void* c, uint64_t epoch, const int32_t* seg_start, const int32_t* seg_src,
+                                const int32_t* seg_dst_row, void* stream) {
+    EpContext* ctx = as_ctx(c);
+    if (!ctx || !ctx->connected) return fail(MOE_B200_ERR_INVALID_ARG, "ep_return_identity: not connected");
+    const EpGeom& g = ctx->g;
+    const int nseg = g.nranks * (g.first[g.rank + 1] - g.first[g.rank]);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaLaunchConfig_t cfg = pdl_config(dim3(sm_count_ep() * 4), dim3(256), 0, s);
+    cudaLaunchAttribute attr = pdl_attr();
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, ep_return_identity_kernel, g, static_cast<char* const*>(ctx->back_dev),
+                                         reinterpret_cast<const uint4*>(ctx->region + g.off_recv), seg_start, seg_src,
+                                         seg_dst_row, nseg);
+    if (err == cudaSuccess) {
+        ep_signal_kernel<<<1, 64, 0, s>>>(g, ctx->peer_dev, g.off_bflag, epoch);
+        err = cudaGetLastError();
+    }
+    return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "ep_return_identity launch");
+}
+
+int moe_b200_ep_ffn_return(void* c, uint64_t epoch, const int32_t* seg_start, const int32_t* seg_expert,
+                           const int32_t* seg_src, const int32_t* seg_dst_row, int I, const void* w_gate_up,
+                           const void* w_down, int dtype, void* h, void* stream) {
+    EpContext* ctx = as_ctx(c);
+    if (!ctx || !ctx->connected) return fail(MOE_B200_ERR_INVALID_ARG, "ep_ffn_return: not connected");
+    const EpGeom& g = ctx->g;
+    const int L = g.first[g.rank + 1] - g.first[g.rank];
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // GEMM 2 writes y over the received rows (GEMM 1 has consumed them) and
+    // forwards each finished tile to the sender's back buffer.
+    int st = grouped_swiglu_impl(ctx->region + g.off_recv, seg_start, seg_expert, g.nranks * L, int(g.recv_cap), g.d,
+                                 I, L, w_gate_up, w_down, dtype, h, ctx->region + g.off_recv, s, ctx->back_dev,
+                                 seg_src, seg_dst_row);
+    if (st != MOE_B200_OK) return st;
+    ep_signal_kernel<<<1, 64, 0, s>>>(g, ctx->peer_dev, g.off_bflag, epoch);
+    cudaError_t err = cudaGetLastError();
+    return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "ep_ffn_return signal");
+}
+
+int moe_b200_ep_combine(void* c, uint64_t epoch, const float* packed_weights, const int32_t* slot_pos, int T,
+                        int dtype, void* out, void* stream) {
+    EpContext* ctx = as_ctx(c);
+    if (!ctx || !ctx->connected) return fail(MOE_B200_ERR_INVALID_ARG, "ep_combine: not connected");
+    const EpGeom& g = ctx->g;
+    if (T < 1 || T > g.max_tokens || !packed_weights || !slot_pos || !out)
+        return fail(MOE_B200_ERR_INVALID_ARG, "ep_combine: need 1 <= T <= max_tokens and all buffers");
+    uint32_t* st = device_status_word();
+    if (!st) return fail(MOE_B200_ERR_CUDA, "ep_combine: device status word unavailable");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    ep_wait_kernel<<<1, 64, 0, s>>>(g, ctx->region, g.off_bflag, epoch, st);
+    cudaError_t err = cudaGetLastError();
+    if (err == cudaSuccess)
+        err = launch_unpermute(ctx->region + g.off_back, packed_weights, slot_pos, T, g.K, g.d, dtype, out, s);
+    return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "ep_combine launch");
+}
+
+}  // extern "C"

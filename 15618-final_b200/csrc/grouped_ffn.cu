@@ -43,7 +43,7 @@ constexpr int kFfnThreads = 192;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kABytes = kTileM * kTileK * 2;  // 16 KB
 constexpr uint32_t kBBytes = kTileN * kTileK * 2;  // 32 KB
-constexpr int kMaxSegments = 2048;  // keeps shared memory under 227 KB
+constexpr int kMaxSegments = 1024;  // keeps shared memory under 227 KB
 
 enum { kEpiSwiGLU = 0, kEpiStore = 1 };
 
@@ -182,7 +182,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                     const int32_t* __restrict__ seg_start, const int32_t* __restrict__ seg_expert,
                     int nseg, int kdim, int b_rows_per_expert, int n_out, int n_blocks,
                     int gate_up_split, uint16_t* __restrict__ out, int64_t out_stride,
-                    uint32_t* __restrict__ dev_status) {
+                    uint32_t* __restrict__ dev_status, char* const* __restrict__ dst_base,
+                    const int32_t* __restrict__ seg_src, const int32_t* __restrict__ seg_dst_row) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte aligned stage buffers (SW128 atoms), control block after them.
     unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -193,6 +194,11 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     int32_t* blk_prefix = reinterpret_cast<int32_t*>(ctl + 1);  // [nseg + 1]
     int32_t* s_start = blk_prefix + (nseg + 1);                 // [nseg + 1] row offsets
     int32_t* s_expert = s_start + (nseg + 1);                   // [nseg] expert of each segment
+    // scatter mode (dst_base != nullptr): row r of segment s is stored at
+    // dst_base[seg_src[s]] + (seg_dst_row[s] + r) rows -- e.g. the back buffer
+    // of the rank that sent the segment's rows
+    int32_t* s_src = s_expert + nseg;                           // [nseg]
+    int32_t* s_dst_row = s_src + nseg;                          // [nseg]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     volatile int* abort_flag = &ctl->abort_flag;
@@ -220,6 +226,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                 const int lo = seg_start[s], hi = seg_start[s + 1];
                 s_start[s] = lo;
                 s_expert[s] = seg_expert ? seg_expert[s] : s;
+                if (dst_base) {
+                    s_src[s] = seg_src[s];
+                    s_dst_row[s] = seg_dst_row[s];
+                }
                 int rows = hi - lo;
                 cnt = rows > 0 ? (rows + kTileM - 1) / kTileM : 0;
             }
@@ -333,6 +343,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             const int seg_rows = s_start[s + 1] - s_start[s];
             const bool row_ok = blk * kTileM + r_in_tile < seg_rows;
             const int64_t row = int64_t(s_start[s]) + blk * kTileM + r_in_tile;
+            uint16_t* out_row = out + row * out_stride;
             const uint32_t t_row = tmem + uint32_t(buf) * kTileN + (uint32_t(quad * 32) << 16);
             if (EPI == kEpiSwiGLU) {
                 // 32 gate + 32 up columns per TMEM round trip
@@ -355,7 +366,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                                 const float u0 = __uint_as_float(ur[hb][2 * q]), u1 = __uint_as_float(ur[hb][2 * q + 1]);
                                 o[q] = pack2<DT>(silu(g0) * u0, silu(g1) * u1);
                             }
-                            uint4* dst = reinterpret_cast<uint4*>(out + row * out_stride + col);
+                            uint4* dst = reinterpret_cast<uint4*>(out_row + col);
                             st_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
                             st_v4(dst + 1, make_uint4(o[4], o[5], o[6], o[7]));
                         }
@@ -377,10 +388,28 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
 #pragma unroll
                             for (int q = 0; q < 8; ++q)
                                 o[q] = pack2<DT>(__uint_as_float(v[q4][2 * q]), __uint_as_float(v[q4][2 * q + 1]));
-                            uint4* dst = reinterpret_cast<uint4*>(out + row * out_stride + col);
+                            uint4* dst = reinterpret_cast<uint4*>(out_row + col);
                             st_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
                             st_v4(dst + 1, make_uint4(o[4], o[5], o[6], o[7]));
                         }
+                    }
+                }
+                if (dst_base) {
+                    // Forward this warp's 32 finished rows (this tile's columns)
+                    // to their destinations, one whole row slice per warp store
+                    // (lane = 16-byte chunk): coalesced writes over NVLink.
+                    __syncwarp();
+                    const int c0 = n * kTileN;
+                    const int ncol = n_out - c0 < kTileN ? n_out - c0 : kTileN;
+                    const int nchunk = ncol / 8;
+                    const int64_t seg_row0 = int64_t(blk) * kTileM + quad * 32;
+                    uint16_t* dbase = reinterpret_cast<uint16_t*>(dst_base[s_src[s]]);
+                    for (int rr = 0; rr < 32; ++rr) {
+                        if (seg_row0 + rr >= seg_rows) break;
+                        const uint16_t* src = out + (int64_t(s_start[s]) + seg_row0 + rr) * out_stride + c0;
+                        uint16_t* dst = dbase + (int64_t(s_dst_row[s]) + seg_row0 + rr) * out_stride + c0;
+                        for (int ch = lane; ch < nchunk; ch += 32)
+                            st_v4(reinterpret_cast<uint4*>(dst) + ch, __ldcg(reinterpret_cast<const uint4*>(src) + ch));
                     }
                 }
             }
@@ -390,6 +419,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         }
     }
 
+    // Stores to another GPU's memory must be visible system-wide before the
+    // flag that announces them (raised by a later kernel in this stream).
+    if (dst_base && warp >= 2) __threadfence_system();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -437,7 +469,7 @@ static bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t c
 }
 
 static size_t ffn_smem_bytes(int nseg) {
-    return 1024 + kStages * (kABytes + kBBytes) + sizeof(FfnSmem) + size_t(3 * nseg + 2) * 4;
+    return 1024 + kStages * (kABytes + kBBytes) + sizeof(FfnSmem) + size_t(5 * nseg + 2) * 4;
 }
 
 static int sm_count_ffn() {
@@ -450,7 +482,8 @@ template <int EPI, int DT>
 static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb_, const int32_t* seg_start,
                                const int32_t* seg_expert, int nseg, int rows, int kdim, int b_rows_per_expert,
                                int n_out, int n_blocks, int split, void* out, int64_t out_stride,
-                               uint32_t* st, cudaStream_t stream) {
+                               uint32_t* st, cudaStream_t stream, char* const* dst_base = nullptr,
+                               const int32_t* seg_src = nullptr, const int32_t* seg_dst_row = nullptr) {
     const size_t smem = ffn_smem_bytes(nseg);
     auto kern = grouped_gemm_kernel<EPI, DT>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -461,7 +494,8 @@ static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb_, co
     if (max_tiles < grid) grid = int(max_tiles > 0 ? max_tiles : 1);
     cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(kFfnThreads), smem, stream);
     return cudaLaunchKernelEx(&cfg, kern, ma, mb_, seg_start, seg_expert, nseg, kdim, b_rows_per_expert, n_out,
-                              n_blocks, split, static_cast<uint16_t*>(out), out_stride, st);
+                              n_blocks, split, static_cast<uint16_t*>(out), out_stride, st, dst_base, seg_src,
+                              seg_dst_row);
 }
 
 int fail(int code, const char* fmt, ...);
@@ -469,10 +503,11 @@ int cuda_fail(cudaError_t err, const char* where);
 
 }  // namespace moe_b200
 
-extern "C" int moe_b200_grouped_swiglu(const void* x, const int32_t* seg_start, const int32_t* seg_expert,
-                                       int nseg, int rows, int d, int I, int E, const void* w_gate_up,
-                                       const void* w_down, int dtype, void* h, void* y, void* stream) {
-    using namespace moe_b200;
+namespace moe_b200 {
+int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* seg_expert, int nseg, int rows,
+                        int d, int I, int E, const void* w_gate_up, const void* w_down, int dtype, void* h,
+                        void* y, cudaStream_t s, char* const* dst_base, const int32_t* seg_src,
+                        const int32_t* seg_dst_row) {
     if (nseg < 1 || rows < 0 || d < 1 || I < 1 || E < 1)
         return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: need nseg>=1, rows>=0, d>=1, I>=1, E>=1");
     if (nseg > kMaxSegments)
@@ -481,11 +516,13 @@ extern "C" int moe_b200_grouped_swiglu(const void* x, const int32_t* seg_start, 
         return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: dtype %d is neither F16 nor BF16", dtype);
     if (d % 16 != 0 || I % 16 != 0)
         return fail(MOE_B200_ERR_UNSUPPORTED, "grouped_swiglu: d and I must be multiples of 16 (d=%d I=%d)", d, I);
-    if (!x || !seg_start || !w_gate_up || !w_down || !h || !y)
+    if (!x || !seg_start || !w_gate_up || !w_down || !h || (!y && !dst_base))
         return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: null pointer");
     const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w_gate_up) |
                          reinterpret_cast<uintptr_t>(w_down) | reinterpret_cast<uintptr_t>(h) |
                          reinterpret_cast<uintptr_t>(y);
+    if (dst_base && (!seg_src || !seg_dst_row))
+        return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: scatter mode needs seg_src and seg_dst_row");
     if (al % 16 != 0) return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: pointers must be 16-byte aligned");
     if (rows == 0) return MOE_B200_OK;
     uint32_t* st = device_status_word();
@@ -496,7 +533,6 @@ extern "C" int moe_b200_grouped_swiglu(const void* x, const int32_t* seg_start, 
         !make_map(&mh, h, rows, I, kTileM, dtype) ||
         !make_map(&mwd, w_down, int64_t(E) * d, I, kTileN, dtype))
         return fail(MOE_B200_ERR_CUDA, "grouped_swiglu: cuTensorMapEncodeTiled failed");
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int nb1 = (I + kTileN / 2 - 1) / (kTileN / 2);
     const int nb2 = (d + kTileN - 1) / kTileN;
     cudaError_t err;
@@ -505,13 +541,21 @@ extern "C" int moe_b200_grouped_swiglu(const void* x, const int32_t* seg_start, 
                                                      I, h, I, st, s);
         if (err == cudaSuccess)
             err = launch_gemm<kEpiStore, MOE_B200_BF16>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0,
-                                                        y, d, st, s);
+                                                        y, d, st, s, dst_base, seg_src, seg_dst_row);
     } else {
         err = launch_gemm<kEpiSwiGLU, MOE_B200_F16>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1,
                                                     I, h, I, st, s);
         if (err == cudaSuccess)
             err = launch_gemm<kEpiStore, MOE_B200_F16>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0,
-                                                       y, d, st, s);
+                                                       y, d, st, s, dst_base, seg_src, seg_dst_row);
     }
     return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "grouped_swiglu launch");
+}
+}  // namespace moe_b200
+
+extern "C" int moe_b200_grouped_swiglu(const void* x, const int32_t* seg_start, const int32_t* seg_expert,
+                                       int nseg, int rows, int d, int I, int E, const void* w_gate_up,
+                                       const void* w_down, int dtype, void* h, void* y, void* stream) {
+    return moe_b200::grouped_swiglu_impl(x, seg_start, seg_expert, nseg, rows, d, I, E, w_gate_up, w_down, dtype,
+                                         h, y, static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr);
 }

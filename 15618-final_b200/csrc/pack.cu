@@ -201,14 +201,6 @@ route_scan_kernel(const int32_t* __restrict__ asgn, int64_t TK, int E, int num_t
     if (tid == kScanThreads - 1) expert_start[E] = warp_off + incl;
 }
 
-// After the route/scan grid has finished (PDL wait done): re-zero its ticket
-// and look-back words so the workspace is ready for the next call.
-__device__ __forceinline__ void rearm_scan_scratch(WsHeader* hdr, uint64_t* status, size_t words) {
-    const size_t gt = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    const size_t nt = size_t(gridDim.x) * blockDim.x;
-    for (size_t i = gt; i < words; i += nt) status[i] = 0;
-    if (gt == 0) hdr->ticket = 0;
-}
 
 // One warp per token; VPL 16-byte vectors per lane per pass over the row.
 template <int VPL>
@@ -440,6 +432,21 @@ static int sm_count() {
     return n > 0 ? n : 148;
 }
 
+// Enqueues the route/scan kernel alone (ranks in the workspace, counts and
+// starts in the outputs); used by launch_pack and by the expert-parallel
+// dispatch.
+cudaError_t launch_route_scan(const int32_t* asgn, int T, int K, int E, int32_t* expert_count,
+                              int32_t* expert_start, void* ws, cudaStream_t stream) {
+    const PackPlan plan = plan_pack(T, K, E);
+    char* base = static_cast<char*>(ws);
+    size_t smem = size_t(kScanWarps + 2) * E * sizeof(int32_t);
+    route_scan_kernel<<<plan.num_tiles, kScanThreads, smem, stream>>>(
+        asgn, int64_t(T) * K, E, plan.num_tiles, reinterpret_cast<WsHeader*>(base),
+        reinterpret_cast<uint64_t*>(base + plan.status_off),
+        reinterpret_cast<int32_t*>(base + plan.rank_off), expert_count, expert_start);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_pack(const void* emb, const int32_t* asgn, const float* wts, int T, int K,
                         int E, int d, void* packed, float* packed_w, int32_t* perm,
                         int32_t* expert_count, int32_t* expert_start, int32_t* slot_pos,
@@ -452,11 +459,9 @@ cudaError_t launch_pack(const void* emb, const int32_t* asgn, const float* wts, 
     const int64_t TK = int64_t(T) * K;
     const size_t words = size_t(plan.num_tiles) * size_t(E);
 
-    size_t smem = size_t(kScanWarps + 2) * E * sizeof(int32_t);
-    route_scan_kernel<<<plan.num_tiles, kScanThreads, smem, stream>>>(
-        asgn, TK, E, plan.num_tiles, hdr, status, rank, expert_count, expert_start);
-    cudaError_t err = cudaGetLastError();
+    cudaError_t err = launch_route_scan(asgn, T, K, E, expert_count, expert_start, ws, stream);
     if (err != cudaSuccess) return err;
+    (void)TK;
 
     const bool vec = (d % 8 == 0) && (reinterpret_cast<uintptr_t>(emb) % 16 == 0) &&
                      (reinterpret_cast<uintptr_t>(packed) % 16 == 0);

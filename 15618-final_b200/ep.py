@@ -24,6 +24,16 @@ def expert_ranges(E: int, N: int) -> List[int]:
     return bounds
 
 
+def balanced_labels(E: int, N: int) -> List[int]:
+    """Expert placement that deals experts round-robin over the ranks: expert e
+    (e = popularity rank, 0 = hottest) gets label first[e % N] + e // N, so
+    rank r owns labels [first[r], first[r+1]) = experts r, r+N, r+2N, ...
+    Routing with relabelled experts is the same as permuting the router's
+    output columns; packed rows stay grouped by owning rank."""
+    b = expert_ranges(E, N)
+    return [b[e % N] + e // N for e in range(E)]
+
+
 def owner_of(E: int, N: int) -> List[int]:
     b = expert_ranges(E, N)
     own = []
@@ -141,3 +151,117 @@ class ExpertParallel:
         out = back[:nsend]
         self.dist.all_to_all_single(out, y[: sum(lay.recv)], lay.send, lay.recv, group=self.group)
         return out
+
+
+class _DeviceArray:
+    """Exposes a raw device allocation to torch (zero copy)."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+class FusedExpertParallel:
+    """Expert parallelism without a collective library on the data path: the
+    packing kernel stores each token row straight into the receive buffer of
+    the rank owning its expert (peer memory over NVLink, mapped with CUDA IPC),
+    the expert's down-GEMM stores its rows straight back into the sender's
+    buffer, and epoch flags in peer memory order the steps.  torch.distributed
+    is used once, to exchange the 64-byte IPC handles.  See include/moe_b200.h
+    (moe_b200_ep_*) for the protocol; replaces the reference's host-synchronised
+    NCCL exchange (apps/bench_prefill.cu:768-807, 889-906).
+
+    Every rank must run the same sequence of steps (epochs advance together)."""
+
+    def __init__(self, E: int, K: int, d: int, max_tokens: int, dtype, group=None, device=None,
+                 timeout_ms: int = 2000):
+        import ctypes
+        import torch
+        import torch.distributed as dist
+        import moe_b200 as mb
+        self.mb = mb
+        self.L_ = mb.lib()
+        self.dist = dist
+        self.group = group
+        if dist.is_available() and dist.is_initialized():
+            self.N, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        else:
+            self.N, self.rank = 1, 0
+        self.E, self.K, self.d, self.dtype = E, K, d, dtype
+        self.bounds = expert_ranges(E, self.N)
+        self.L = self.bounds[self.rank + 1] - self.bounds[self.rank]
+        self.device = device
+        first = (ctypes.c_int32 * (self.N + 1))(*self.bounds)
+        self.ctx = ctypes.c_void_p()
+        mb._check(self.L_.moe_b200_ep_create(self.N, self.rank, E, K, d, max_tokens, first, timeout_ms,
+                                             ctypes.byref(self.ctx)), "ep_create")
+        h = (ctypes.c_uint8 * 64)()
+        mb._check(self.L_.moe_b200_ep_ipc_handle(self.ctx, h), "ep_ipc_handle")
+        mine = torch.tensor(list(h), dtype=torch.uint8, device=device)
+        if self.N > 1:
+            allh = torch.empty(self.N * 64, dtype=torch.uint8, device=device)
+            dist.all_gather_into_tensor(allh, mine, group=group)
+        else:
+            allh = mine
+        buf = (ctypes.c_uint8 * (self.N * 64))(*allh.cpu().tolist())
+        mb._check(self.L_.moe_b200_ep_connect(self.ctx, buf), "ep_connect")
+        self.epoch = 0
+        nseg = self.N * self.L
+        mk = lambda n: torch.empty(n, dtype=torch.int32, device=device)
+        self.seg_start, self.seg_expert, self.seg_src, self.seg_dst_row = mk(nseg + 1), mk(nseg), mk(nseg), mk(nseg)
+        self.recv_cap = int(self.L_.moe_b200_ep_recv_capacity(self.ctx))
+
+    def _s(self, stream):
+        return self.mb._stream_handle(stream)
+
+    def recv_rows(self):
+        import torch
+        p = self.L_.moe_b200_ep_recv_rows(self.ctx)
+        return torch.as_tensor(_DeviceArray(p, (self.recv_cap, self.d), "<i2"), device=self.device).view(self.dtype)
+
+    def dispatch(self, emb, asgn, wts, workspace, out, stream=None):
+        """Starts a step: pack + peer-store dispatch.  `out` is a moe_b200.PackResult
+        (its packed buffer is not written: rows go straight to their owners)."""
+        self.epoch += 1
+        T = emb.shape[0]
+        p = self.mb._ptr
+        self.mb._check(self.L_.moe_b200_ep_dispatch(
+            self.ctx, self.epoch, p(emb), p(asgn), p(wts), T, p(out.packed_weights), p(out.perm),
+            p(out.expert_count), p(out.expert_start), p(out.slot_pos), workspace.buf.data_ptr(), workspace.nbytes,
+            self._s(stream)), "ep_dispatch")
+
+    def receive(self, stream=None):
+        p = self.mb._ptr
+        self.mb._check(self.L_.moe_b200_ep_receive(self.ctx, self.epoch, p(self.seg_start), p(self.seg_expert),
+                                                   p(self.seg_src), p(self.seg_dst_row), self._s(stream)),
+                       "ep_receive")
+
+    def return_identity(self, stream=None):
+        p = self.mb._ptr
+        self.mb._check(self.L_.moe_b200_ep_return_identity(self.ctx, self.epoch, p(self.seg_start),
+                                                           p(self.seg_src), p(self.seg_dst_row), self._s(stream)),
+                       "ep_return_identity")
+
+    def ffn_return(self, w_gate_up, w_down, h, stream=None):
+        """Grouped SwiGLU on the received rows (local experts' weights
+        [L, 2I, d] / [L, d, I]); h: [recv_capacity, I] scratch."""
+        p = self.mb._ptr
+        I = w_down.shape[2]
+        self.mb._check(self.L_.moe_b200_ep_ffn_return(
+            self.ctx, self.epoch, p(self.seg_start), p(self.seg_expert), p(self.seg_src), p(self.seg_dst_row), I,
+            p(w_gate_up), p(w_down), self.mb.dtype_code(self.dtype), p(h), self._s(stream)), "ep_ffn_return")
+
+    def combine(self, packed_weights, slot_pos, T, out, stream=None):
+        p = self.mb._ptr
+        self.mb._check(self.L_.moe_b200_ep_combine(self.ctx, self.epoch, p(packed_weights), p(slot_pos), T,
+                                                   self.mb.dtype_code(self.dtype), p(out), self._s(stream)),
+                       "ep_combine")
+
+    def close(self):
+        if self.ctx:
+            import torch
+            torch.cuda.synchronize()
+            if self.N > 1:
+                self.dist.barrier(group=self.group)
+            self.L_.moe_b200_ep_destroy(self.ctx)
+            self.ctx = None

@@ -78,6 +78,32 @@ def lib() -> ctypes.CDLL:
     L.moe_b200_grouped_swiglu.argtypes = [vp, vp, vp, cint, cint, cint, cint, cint, vp, vp, cint, vp, vp, vp]
     L.moe_b200_ep_layout.restype = cint
     L.moe_b200_ep_layout.argtypes = [vp, cint, cint, cint, ctypes.POINTER(ctypes.c_int32), vp, vp, vp, vp, vp]
+    u64 = ctypes.c_uint64
+    L.moe_b200_ep_create.restype = cint
+    L.moe_b200_ep_create.argtypes = [cint, cint, cint, cint, cint, cint, ctypes.POINTER(ctypes.c_int32), cint,
+                                     ctypes.POINTER(vp)]
+    L.moe_b200_ep_destroy.restype = cint
+    L.moe_b200_ep_destroy.argtypes = [vp]
+    L.moe_b200_ep_ipc_handle.restype = cint
+    L.moe_b200_ep_ipc_handle.argtypes = [vp, vp]
+    L.moe_b200_ep_connect.restype = cint
+    L.moe_b200_ep_connect.argtypes = [vp, vp]
+    L.moe_b200_ep_recv_rows.restype = vp
+    L.moe_b200_ep_recv_rows.argtypes = [vp]
+    L.moe_b200_ep_back_rows.restype = vp
+    L.moe_b200_ep_back_rows.argtypes = [vp]
+    L.moe_b200_ep_recv_capacity.restype = ctypes.c_int64
+    L.moe_b200_ep_recv_capacity.argtypes = [vp]
+    L.moe_b200_ep_dispatch.restype = cint
+    L.moe_b200_ep_dispatch.argtypes = [vp, u64, vp, vp, vp, cint, vp, vp, vp, vp, vp, vp, sz, vp]
+    L.moe_b200_ep_receive.restype = cint
+    L.moe_b200_ep_receive.argtypes = [vp, u64, vp, vp, vp, vp, vp]
+    L.moe_b200_ep_return_identity.restype = cint
+    L.moe_b200_ep_return_identity.argtypes = [vp, u64, vp, vp, vp, vp]
+    L.moe_b200_ep_ffn_return.restype = cint
+    L.moe_b200_ep_ffn_return.argtypes = [vp, u64, vp, vp, vp, vp, cint, vp, vp, cint, vp, vp]
+    L.moe_b200_ep_combine.restype = cint
+    L.moe_b200_ep_combine.argtypes = [vp, u64, vp, vp, cint, cint, vp, vp]
     L.moe_b200_unpermute.restype = cint
     L.moe_b200_unpermute.argtypes = [vp, vp, vp, cint, cint, cint, cint, vp, vp]
     _lib = L

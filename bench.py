@@ -49,6 +49,11 @@ def parse():
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
+                    help="N>1 expert placement: popularity dealt round-robin over ranks (default) or the "
+                         "reference's contiguous ranges")
+    ap.add_argument("--ep", default="fused", choices=["fused", "nccl"],
+                    help="N>1 exchange: fused peer-store kernels (default) or NCCL AllToAllv")
     return ap.parse_args()
 
 
@@ -66,6 +71,7 @@ def config_json(c, n, l2_note):
         "expert": "identity",
         "pipeline": "pack -> unpermute" if n == 1 else "pack -> AllToAllv -> identity -> AllToAllv -> unpermute",
         "parallelism": f"ep{n}" if n > 1 else "single-gpu",
+        "placement": c.get("placement", "n/a"),
         "l2": l2_note,
     }
 
@@ -318,6 +324,7 @@ def gpu_arm(args):
 
     c = workload(args.config, rank)
     c["name"] = args.config
+    c["placement"] = args.placement if world > 1 else "n/a"
     layer = "I" in c                       # c5: the full layer with SwiGLU experts
     if layer:
         # the layer's T tokens are split over the ranks (apps/bench_prefill.cu:341)
@@ -328,6 +335,11 @@ def gpu_arm(args):
     TK = T * K
     tdtype = getattr(torch, c["dtype"])
     asgn_np, wts_np = routing.gen_routing(T, K, E, c["dist"], c["seed"])
+    label = list(range(E))
+    if world > 1 and args.placement == "balanced":
+        label = ep.balanced_labels(E, world)
+        asgn_np = np.asarray(label, dtype=np.int32)[asgn_np]
+    orig_of = {l: e for e, l in enumerate(label)}
     emb = routing.gen_rows(T, d, c["dtype"], c["seed"], device=dev)
     asgn = torch.from_numpy(asgn_np).to(dev)
     wts = torch.from_numpy(wts_np).to(dev)
@@ -347,18 +359,24 @@ def gpu_arm(args):
             # rank count uses the same weights (apps/bench_prefill.cu:432-439)
             wgu = torch.empty((hi - lo, 2 * I, d), dtype=tdtype, device=dev)
             wdn = torch.empty((hi - lo, d, I), dtype=tdtype, device=dev)
-            for j, e in enumerate(range(lo, hi)):
+            for j, lab in enumerate(range(lo, hi)):
                 g = torch.Generator(device=dev)
-                g.manual_seed(1000 + e)
+                g.manual_seed(1000 + orig_of[lab])
                 wgu[j] = (torch.randn((2 * I, d), generator=g, device=dev) * 0.02).to(tdtype)
                 wdn[j] = (torch.randn((d, I), generator=g, device=dev) * 0.02).to(tdtype)
             cap = world * TK if world > 1 else TK
             h_buf = torch.empty((cap, I), dtype=tdtype, device=dev)
             y_buf = torch.empty((cap, d), dtype=tdtype, device=dev)
-    if world > 1:
+    fused = world > 1 and args.ep == "fused"
+    if world > 1 and not fused:
         epx = ep.ExpertParallel(E, device=dev)
         recv_buf = torch.empty((world * TK, d), dtype=tdtype, device=dev)
         back_buf = torch.empty((TK, d), dtype=tdtype, device=dev)
+    if fused:
+        with torch.cuda.stream(stream):
+            fep = ep.FusedExpertParallel(E, K, d, T, tdtype, device=dev, timeout_ms=5000)
+            if layer:
+                h_buf = torch.empty((fep.recv_cap, c["I"]), dtype=tdtype, device=dev)
 
     def step(split=False):
         """One pass.  Returns CUDA events recorded on the launching stream: the
@@ -368,6 +386,20 @@ def gpu_arm(args):
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(6 if split else 2)]
         mark = (lambda i: evs[i].record(stream)) if split else (lambda i: None)
         evs[0].record(stream)
+        if fused:
+            fep.dispatch(emb, asgn, wts, ws, bufs, stream=stream)
+            mark(1)
+            fep.receive(stream=stream)
+            mark(2)
+            if layer:
+                fep.ffn_return(wgu, wdn, h_buf, stream=stream)
+            else:
+                fep.return_identity(stream=stream)
+            mark(3)
+            mark(4)
+            fep.combine(bufs.packed_weights, bufs.slot_pos, T, out, stream=stream)
+            evs[-1].record(stream)
+            return evs
         mb.pack(emb, asgn, wts, E, workspace=ws, out=bufs, stream=stream)
         mark(1)
         if world > 1:
@@ -452,6 +484,11 @@ def gpu_arm(args):
         kernels = ["route_scan_kernel", "pack_rows_bulk_kernel", "unpermute_bulk_kernel"]
         if layer:
             kernels[2:2] = ["grouped_gemm_kernel<SwiGLU>", "grouped_gemm_kernel<store>"]
+        if fused:
+            kernels = ["route_scan_kernel", "ep_publish_kernel", "ep_pack_dispatch_kernel", "ep_receive_kernel"] + \
+                (["grouped_gemm_kernel<SwiGLU>", "grouped_gemm_kernel<store, peer scatter>"] if layer
+                 else ["ep_return_identity_kernel"]) + ["ep_signal_kernel", "ep_wait_kernel",
+                                                        "unpermute_bulk_kernel"]
         line = {
             "metric": METRIC_LAYER if layer else METRIC,
             "unit": "us" if layer else UNIT,
@@ -471,8 +508,8 @@ def gpu_arm(args):
                           "note": "max over ranks of the per-rank means, from a separate loop with events "
                                   "between the stages (costs the PDL overlap); the headline step has events "
                                   "at its boundaries only"},
-            "gpu_launches": len(kernels) * args.steps + (args.steps if world > 1 else 0),
-            "kernels_per_step": kernels + (["ep_layout_kernel"] if world > 1 else []),
+            "gpu_launches": len(kernels) * args.steps + (args.steps if world > 1 and not fused else 0),
+            "kernels_per_step": kernels + (["ep_layout_kernel"] if world > 1 and not fused else []),
             "clocks": clk.summary(),
         }
         if layer:
@@ -507,7 +544,12 @@ def gpu_arm(args):
             }
         if world > 1:
             line["ep"] = {"experts_per_rank": [bounds[g + 1] - bounds[g] for g in range(world)],
-                          "collectives": "NCCL all_gather (counts) + 2 x all_to_all_single (rows)"}
+                          "placement": args.placement + (" (expert e -> rank e % N by popularity rank)"
+                                                         if args.placement == "balanced" else ""),
+                          "exchange": ("fused: pack stores rows into the owners' receive buffers over NVLink, "
+                                       "the expert stores them back into the senders' buffers; epoch flags in "
+                                       "peer memory, no collective library and no host sync on the data path")
+                          if fused else "NCCL all_gather (counts) + 2 x all_to_all_single (rows)"}
         if e2e is not None:
             line["e2e"] = e2e
         if world == 1 and not args.no_cpu_baseline and not layer:
@@ -520,6 +562,8 @@ def gpu_arm(args):
                           f"{host_cores()}"}
         print(json.dumps(line), flush=True)
 
+    if fused:
+        fep.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -152,7 +152,7 @@ int moe_b200_unpermute(const void* y, const float* packed_weights, const int32_t
  *   w_down     [E, d, I]       row c: output column c over the I inner features
  *   h          [rows, I]       out: the SwiGLU intermediate
  *   y          [rows, d]       out: expert outputs, in packed order
- * d and I multiples of 16; all pointers 16-byte aligned; nseg <= 2048.
+ * d and I multiples of 16; all pointers 16-byte aligned; nseg <= 1024.
  * Replaces the per-expert cublasHgemm loop (apps/bench_e2e.cu:274-301,
  * apps/bench_prefill.cu:854-884) and the CUTLASS sm80 GemmGrouped FFN
  * (apps/bench_prefill.cu:68-202, 812-852), which have no activation and need
@@ -183,6 +183,55 @@ int moe_b200_ep_layout(const int32_t* all_counts, int nranks, int E, int rank,
                        const int32_t* expert_first /* host */, int32_t* seg_start,
                        int32_t* seg_expert, int32_t* send_counts, int32_t* recv_counts,
                        void* stream);
+
+/* ------------------------------ fused expert parallel over peer memory ---- */
+
+/* One process per GPU.  A context owns this rank's symmetric region (receive
+ * rows for up to nranks*max_tokens*K rows, back rows, counts inbox, epoch
+ * flags), which the peers map through CUDA IPC.  Lifecycle:
+ *   moe_b200_ep_create -> moe_b200_ep_ipc_handle (64 bytes) -> exchange the
+ *   handles between the ranks (any host channel) -> moe_b200_ep_connect with
+ *   all nranks handles in rank order -> steps -> barrier -> moe_b200_ep_destroy.
+ * A step, with the same epoch on every rank (1, 2, 3, ...), enqueued on one
+ * stream and never blocking the host:
+ *   moe_b200_ep_dispatch         route/scan, publish counts to every peer,
+ *                                 store every token row straight into the
+ *                                 receive buffer of the rank owning its expert
+ *   moe_b200_ep_receive           wait for all senders; segment table of the
+ *                                 receive buffer (seg_* arrays of nranks*L(+1),
+ *                                 L = this rank's experts)
+ *   moe_b200_ep_ffn_return        grouped SwiGLU on the received rows whose
+ *                                 down-GEMM stores every row straight into
+ *                                 the sender's back buffer
+ *     or moe_b200_ep_return_identity   (identity expert)
+ *   moe_b200_ep_combine           wait for all returns; weighted unpermute
+ * Replaces the reference's AllGather -> D2H -> host offsets -> grouped
+ * ncclSend/ncclRecv dispatch and combine (apps/bench_prefill.cu:768-807,
+ * 889-906).  Waits are bounded by timeout_ms and report
+ * MOE_B200_DEV_WAIT_TIMEOUT through moe_b200_device_status().              */
+int moe_b200_ep_create(int nranks, int rank, int E, int K, int d, int max_tokens,
+                       const int32_t* expert_first /* host, nranks+1 */, int timeout_ms,
+                       void** ctx /* host, out */);
+int moe_b200_ep_destroy(void* ctx);
+int moe_b200_ep_ipc_handle(void* ctx, void* handle /* host, 64 bytes out */);
+int moe_b200_ep_connect(void* ctx, const void* handles /* host, nranks*64 bytes */);
+void* moe_b200_ep_recv_rows(void* ctx);
+void* moe_b200_ep_back_rows(void* ctx);
+int64_t moe_b200_ep_recv_capacity(void* ctx);
+int moe_b200_ep_dispatch(void* ctx, uint64_t epoch, const void* emb, const int32_t* asgn,
+                         const float* wts, int T, float* packed_weights, int32_t* perm,
+                         int32_t* expert_count, int32_t* expert_start, int32_t* slot_pos,
+                         void* workspace, size_t workspace_bytes, void* stream);
+int moe_b200_ep_receive(void* ctx, uint64_t epoch, int32_t* seg_start, int32_t* seg_expert,
+                        int32_t* seg_src, int32_t* seg_dst_row, void* stream);
+int moe_b200_ep_return_identity(void* ctx, uint64_t epoch, const int32_t* seg_start,
+                                const int32_t* seg_src, const int32_t* seg_dst_row, void* stream);
+int moe_b200_ep_ffn_return(void* ctx, uint64_t epoch, const int32_t* seg_start,
+                           const int32_t* seg_expert, const int32_t* seg_src,
+                           const int32_t* seg_dst_row, int I, const void* w_gate_up,
+                           const void* w_down, int dtype, void* h, void* stream);
+int moe_b200_ep_combine(void* ctx, uint64_t epoch, const float* packed_weights,
+                        const int32_t* slot_pos, int T, int dtype, void* out, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

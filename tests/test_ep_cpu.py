@@ -23,6 +23,21 @@ import oracle
 import routing
 
 
+def join_all(ctx, seconds):
+    """Waits for every spawned rank (ProcessContext.join returns after the
+    first one exits); kills what is still running at the deadline and
+    returns the ranks that had to be killed."""
+    import time
+    deadline = time.time() + seconds
+    while not ctx.join(timeout=max(1.0, deadline - time.time())):
+        if time.time() > deadline:
+            break
+    alive = [p for p in ctx.processes if p.is_alive()]
+    for p in alive:
+        p.kill()
+    return alive
+
+
 def free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -112,10 +127,7 @@ def test_ep_peer_failure_ends_in_error_not_hang():
     with mp.Manager() as m:
         results = m.dict()
         ctx = mp.spawn(_failing_worker, args=(world, port, results), nprocs=world, join=False)
-        ctx.join(timeout=120)
-        for p in ctx.processes:
-            if p.is_alive():
-                p.kill()
+        join_all(ctx, 120)
         res = dict(results)
     assert res.get(1) == "left"
     assert str(res.get(0, "")).startswith("error"), res
@@ -140,3 +152,22 @@ def test_layout_reference_matches_definition():
     assert ep.expert_ranges(60, 8) == [0, 8, 16, 24, 32, 39, 46, 53, 60]
     with pytest.raises(ValueError):
         ep.expert_ranges(3, 4)
+
+
+def test_balanced_placement_is_a_permutation_that_spreads_load():
+    for E, N in [(8, 2), (60, 8), (64, 4), (5, 2)]:
+        lab = ep.balanced_labels(E, N)
+        assert sorted(lab) == list(range(E))
+        b = ep.expert_ranges(E, N)
+        for e in range(E):  # expert e lands on rank e % N
+            assert b[e % N] <= lab[e] < b[e % N + 1]
+    # Zipf routing: the hottest rank's share drops with the balanced placement
+    E, N = 60, 8
+    asgn, _ = routing.gen_routing(8192, 4, E, "zipf", seed=0)
+    b = ep.expert_ranges(E, N)
+    def shares(a):
+        c = np.bincount(a.reshape(-1), minlength=E)
+        return [c[b[r]:b[r + 1]].sum() / c.sum() for r in range(N)]
+    contiguous = shares(asgn)
+    balanced = shares(np.asarray(ep.balanced_labels(E, N))[asgn])
+    assert max(balanced) < 0.5 * max(contiguous)
