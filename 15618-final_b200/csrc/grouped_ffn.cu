@@ -183,7 +183,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                     int nseg, int kdim, int b_rows_per_expert, int n_out, int n_blocks,
                     int gate_up_split, uint16_t* __restrict__ out, int64_t out_stride,
                     uint32_t* __restrict__ dev_status, char* const* __restrict__ dst_base,
-                    const int32_t* __restrict__ seg_src, const int32_t* __restrict__ seg_dst_row) {
+                    const int32_t* __restrict__ seg_src, const int32_t* __restrict__ seg_dst_row,
+                    int seg_groups) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte aligned stage buffers (SW128 atoms), control block after them.
     unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -202,6 +203,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     volatile int* abort_flag = &ctl->abort_flag;
+    const int G = seg_groups > 1 ? seg_groups : 1;
+    const int Lg = nseg / G;
 
     // Set-up: barriers, block prefix over segments, TMEM.
     if (threadIdx.x == 0) {
@@ -217,20 +220,26 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         mbar_fence_init();
     }
     if (warp == 0) {
-        // blk_prefix[s] = number of 128-row blocks in segments < s
+        // Tiles walk the segments in "tile order": with seg_groups = G > 1 the
+        // nseg = G * L segments (stored group-major: group q, item j at q*L+j)
+        // are visited item-major (j*G + q), so consecutive row blocks share an
+        // expert and rotate over the groups (the senders, whose buffers the
+        // scatter epilogue writes to).  blk_prefix[i] = row blocks of the
+        // segments before tile-order position i.
         int run = 0;
         for (int s0 = 0; s0 < nseg; s0 += 32) {
-            int s = s0 + lane;
+            int i = s0 + lane;
             int cnt = 0;
-            if (s < nseg) {
-                const int lo = seg_start[s], hi = seg_start[s + 1];
-                s_start[s] = lo;
-                s_expert[s] = seg_expert ? seg_expert[s] : s;
+            if (i < nseg) {
+                const int lo = seg_start[i];
+                s_start[i] = lo;
+                s_expert[i] = seg_expert ? seg_expert[i] : i;
                 if (dst_base) {
-                    s_src[s] = seg_src[s];
-                    s_dst_row[s] = seg_dst_row[s];
+                    s_src[i] = seg_src[i];
+                    s_dst_row[i] = seg_dst_row[i];
                 }
-                int rows = hi - lo;
+                const int nat = G > 1 ? (i % G) * Lg + i / G : i;  // segment at tile-order position i
+                const int rows = seg_start[nat + 1] - seg_start[nat];
                 cnt = rows > 0 ? (rows + kTileM - 1) / kTileM : 0;
             }
             int incl = cnt;
@@ -239,7 +248,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                 int v = __shfl_up_sync(0xffffffffu, incl, o);
                 if (lane >= o) incl += v;
             }
-            if (s < nseg) blk_prefix[s] = run + incl - cnt;
+            if (i < nseg) blk_prefix[i] = run + incl - cnt;
             run += __shfl_sync(0xffffffffu, incl, 31);
         }
         if (lane == 0) {
@@ -273,9 +282,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             uint32_t it = 0;
             for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
                 const int g = tile / n_blocks, n = tile % n_blocks;
-                const int s = find_segment(blk_prefix, nseg, g);
+                const int ti = find_segment(blk_prefix, nseg, g);
+                const int s = G > 1 ? (ti % G) * Lg + ti / G : ti;
                 const int e = s_expert[s];
-                const int row0 = s_start[s] + (g - blk_prefix[s]) * kTileM;
+                const int row0 = s_start[s] + (g - blk_prefix[ti]) * kTileM;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const int st = int(it % kStages);
                     if (!wait_or_abort(&ctl->empty[st], ((it / kStages) & 1u) ^ 1u, abort_flag, dev_status))
@@ -338,8 +348,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             if (!wait_or_abort(&ctl->tmem_full[buf], (j >> 1) & 1u, abort_flag, dev_status)) break;
             tc_fence_after();
             const int g = tile / n_blocks, n = tile % n_blocks;
-            const int s = find_segment(blk_prefix, nseg, g);
-            const int blk = g - blk_prefix[s];
+            const int ti = find_segment(blk_prefix, nseg, g);
+            const int s = G > 1 ? (ti % G) * Lg + ti / G : ti;
+            const int blk = g - blk_prefix[ti];
             const int seg_rows = s_start[s + 1] - s_start[s];
             const bool row_ok = blk * kTileM + r_in_tile < seg_rows;
             const int64_t row = int64_t(s_start[s]) + blk * kTileM + r_in_tile;
@@ -483,7 +494,8 @@ static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb_, co
                                const int32_t* seg_expert, int nseg, int rows, int kdim, int b_rows_per_expert,
                                int n_out, int n_blocks, int split, void* out, int64_t out_stride,
                                uint32_t* st, cudaStream_t stream, char* const* dst_base = nullptr,
-                               const int32_t* seg_src = nullptr, const int32_t* seg_dst_row = nullptr) {
+                               const int32_t* seg_src = nullptr, const int32_t* seg_dst_row = nullptr,
+                               int seg_groups = 1) {
     const size_t smem = ffn_smem_bytes(nseg);
     auto kern = grouped_gemm_kernel<EPI, DT>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -495,7 +507,7 @@ static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb_, co
     cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(kFfnThreads), smem, stream);
     return cudaLaunchKernelEx(&cfg, kern, ma, mb_, seg_start, seg_expert, nseg, kdim, b_rows_per_expert, n_out,
                               n_blocks, split, static_cast<uint16_t*>(out), out_stride, st, dst_base, seg_src,
-                              seg_dst_row);
+                              seg_dst_row, seg_groups);
 }
 
 int fail(int code, const char* fmt, ...);
@@ -507,7 +519,7 @@ namespace moe_b200 {
 int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* seg_expert, int nseg, int rows,
                         int d, int I, int E, const void* w_gate_up, const void* w_down, int dtype, void* h,
                         void* y, cudaStream_t s, char* const* dst_base, const int32_t* seg_src,
-                        const int32_t* seg_dst_row) {
+                        const int32_t* seg_dst_row, int seg_groups) {
     if (nseg < 1 || rows < 0 || d < 1 || I < 1 || E < 1)
         return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: need nseg>=1, rows>=0, d>=1, I>=1, E>=1");
     if (nseg > kMaxSegments)
@@ -538,16 +550,16 @@ int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* 
     cudaError_t err;
     if (dtype == MOE_B200_BF16) {
         err = launch_gemm<kEpiSwiGLU, MOE_B200_BF16>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1,
-                                                     I, h, I, st, s);
+                                                     I, h, I, st, s, nullptr, nullptr, nullptr, seg_groups);
         if (err == cudaSuccess)
             err = launch_gemm<kEpiStore, MOE_B200_BF16>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0,
-                                                        y, d, st, s, dst_base, seg_src, seg_dst_row);
+                                                        y, d, st, s, dst_base, seg_src, seg_dst_row, seg_groups);
     } else {
         err = launch_gemm<kEpiSwiGLU, MOE_B200_F16>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1,
-                                                    I, h, I, st, s);
+                                                    I, h, I, st, s, nullptr, nullptr, nullptr, seg_groups);
         if (err == cudaSuccess)
             err = launch_gemm<kEpiStore, MOE_B200_F16>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0,
-                                                       y, d, st, s, dst_base, seg_src, seg_dst_row);
+                                                       y, d, st, s, dst_base, seg_src, seg_dst_row, seg_groups);
     }
     return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "grouped_swiglu launch");
 }
@@ -557,5 +569,5 @@ extern "C" int moe_b200_grouped_swiglu(const void* x, const int32_t* seg_start, 
                                        int nseg, int rows, int d, int I, int E, const void* w_gate_up,
                                        const void* w_down, int dtype, void* h, void* y, void* stream) {
     return moe_b200::grouped_swiglu_impl(x, seg_start, seg_expert, nseg, rows, d, I, E, w_gate_up, w_down, dtype,
-                                         h, y, static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr);
+                                         h, y, static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr, 1);
 }
