@@ -71,9 +71,6 @@ route_scan_kernel(const int32_t* __restrict__ asgn, int64_t TK, int E, int num_t
                   WsHeader* __restrict__ hdr, uint64_t* __restrict__ status,
                   int32_t* __restrict__ rank, int32_t* __restrict__ expert_count,
                   int32_t* __restrict__ expert_start) {
-    // Let the row-copy kernel get resident while this one scans.
-    pdl_launch_dependents();
-
     extern __shared__ int32_t smem[];
     int32_t* hist = smem;                        // [kScanWarps][E]
     int32_t* tile_excl = smem + kScanWarps * E;  // [E] exclusive prefix of this tile
@@ -124,6 +121,9 @@ route_scan_kernel(const int32_t* __restrict__ asgn, int64_t TK, int E, int num_t
         r[c] = b + __popc(peers & lt);
     }
     __syncthreads();
+    // The assignments are in registers: let the row-copy kernel start its
+    // row prefetch now (its loads would otherwise queue ahead of ours).
+    pdl_launch_dependents();
 
     // Per expert: exclusive prefix over the tile's warps; publish the tile
     // aggregate (tile 0 publishes its inclusive prefix directly).
@@ -141,18 +141,19 @@ route_scan_kernel(const int32_t* __restrict__ asgn, int64_t TK, int E, int num_t
     }
 
     // Decoupled look-back, one thread per expert: predecessor words are loaded
-    // 8 at a time; aggregates are summed until an inclusive prefix is found.
+    // kWindow at a time; aggregates are summed until an inclusive prefix.
+    constexpr int kWindow = 8;
     for (int x = tid; x < E; x += kScanThreads) {
         int32_t excl = 0;
         int j = tile - 1;
         bool found = tile == 0;
         while (!found) {
-            uint64_t w8[8];
+            uint64_t w8[kWindow];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+            for (int i = 0; i < kWindow; ++i)
                 w8[i] = (j - i >= 0) ? ld_relaxed_u64(status + size_t(j - i) * E + x) : kFlagInclusive;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+            for (int i = 0; i < kWindow; ++i) {
                 if (!found) {
                     uint64_t w = w8[i];
                     if (j - i >= 0 && (w >> 32) == 0) w = wait_status(status + size_t(j - i) * E + x, hdr);
@@ -160,7 +161,7 @@ route_scan_kernel(const int32_t* __restrict__ asgn, int64_t TK, int E, int num_t
                     if ((w >> 32) == 2) found = true;
                 }
             }
-            j -= 8;
+            j -= kWindow;
         }
         tile_excl[x] = excl;
         if (tile > 0)
