@@ -539,8 +539,8 @@ int moe_b200_ep_ffn_return(void* c, uint64_t epoch, const int32_t* seg_start, co
     const EpGeom& g = ctx->g;
     const int L = g.first[g.rank + 1] - g.first[g.rank];
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // GEMM 2 writes y over the received rows (GEMM 1 has consumed them) and
-    // forwards each finished tile to the sender's back buffer.
+    // GEMM 2's epilogue stores each finished tile straight into the back
+    // buffer of the rank that sent its rows (scatter mode).
     int st = grouped_swiglu_impl(ctx->region + g.off_recv, seg_start, seg_expert, g.nranks * L, int(g.recv_cap), g.d,
                                  I, L, w_gate_up, w_down, dtype, h, ctx->region + g.off_recv, s, ctx->back_dev,
                                  seg_src, seg_dst_row, g.nranks);

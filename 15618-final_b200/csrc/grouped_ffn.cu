@@ -14,13 +14,23 @@
 // activation; this one is SwiGLU (gate, up, down).
 //
 // One persistent kernel, one CTA per SM, 6 warps:
-//   warp 0     TMA producer: A tile (128 rows x 64 K) + B tile (256 rows x 64 K)
-//              per stage, 128-byte swizzle, kStages stages
+//   warp 0     TMA producer: A tile (128 rows x 64 K) + B tile per stage,
+//              128-byte swizzle
 //   warp 1     allocates TMEM (512 columns = two 128x256 fp32 accumulators)
-//              and issues tcgen05.mma (M=128, N=256, K=16) from one lane
+//              and issues tcgen05.mma (N=256, K=16) from one lane
 //   warps 2-5  epilogue: tcgen05.ld of their 32-lane quadrant, SwiGLU or
 //              plain conversion, 16-byte stores
-// Tiles are (segment, 128-row block, N block), N fastest, so concurrent CTAs
+// Two CTA-group variants share the code:
+//   CG=1  one SM per 128 x 256 tile, B tile of 256 rows, 4 stages
+//   CG=2  (default) an SM pair (cluster of 2) per 256 x 256 tile:
+//         tcgen05.mma.cta_group::2 with M=256 issued by the pair leader,
+//         each CTA loading its own 128 A rows and half of the B rows, so
+//         each SM stages 32 KB per K step instead of 48 KB and keeps 6
+//         stages in flight; the TMA of both CTAs completes on the leader's
+//         barrier, MMA completion is committed to both CTAs' barriers, and
+//         the epilogue warps of both CTAs release the accumulator to the
+//         leader.
+// Tiles are (segment, row block, N block), N fastest, so concurrent CTAs
 // share the A block and the expert's weights in L2.  Every wait is bounded;
 // on expiry the CTA records MOE_B200_DEV_WAIT_TIMEOUT, raises a CTA-wide abort
 // flag so the other roles stop waiting, and still frees its TMEM.
@@ -29,6 +39,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -38,11 +50,19 @@ namespace moe_b200 {
 constexpr int kTileM = 128;
 constexpr int kTileN = 256;
 constexpr int kTileK = 64;  // 64 x 16-bit = one 128-byte swizzle row
-constexpr int kStages = 4;
 constexpr int kFfnThreads = 192;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kABytes = kTileM * kTileK * 2;  // 16 KB
-constexpr uint32_t kBBytes = kTileN * kTileK * 2;  // 32 KB
+constexpr uint32_t kABytes = kTileM * kTileK * 2;  // 16 KB: one CTA's A rows per stage
+// Per-CTA stage geometry for CTA group CG (1: one SM per tile; 2: an SM pair
+// computes a 256-row tile with tcgen05.mma.cta_group::2, each CTA holding
+// 128 rows of A and half of the 256 B rows).
+template <int CG> struct Geo {
+    static constexpr int kBRows = kTileN / CG;                 // B rows held per CTA
+    static constexpr uint32_t kBBytes = kBRows * kTileK * 2;   // 32 KB / 16 KB
+    static constexpr int kStages = CG == 1 ? 4 : 6;            // 192 KB either way
+    static constexpr int kBlockRows = kTileM * CG;             // rows per tile
+};
+constexpr int kMaxStages = 6;
 constexpr int kMaxSegments = 1024;  // keeps shared memory under 227 KB
 
 enum { kEpiSwiGLU = 0, kEpiStore = 1 };
@@ -63,9 +83,9 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
 
 // Instruction descriptor, kind::f16: fp32 accumulate, A/B fp16 (0) or bf16
 // (1), both K-major, M = 128, N = 256.
-__host__ __device__ constexpr uint32_t umma_idesc(int ab_format) {
+__host__ __device__ constexpr uint32_t umma_idesc(int ab_format, int m = kTileM) {
     return (1u << 4) | (uint32_t(ab_format) << 7) | (uint32_t(ab_format) << 10) |
-           (uint32_t(kTileN >> 3) << 17) | (uint32_t(kTileM >> 4) << 24);
+           (uint32_t(kTileN >> 3) << 17) | (uint32_t(m >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
@@ -84,6 +104,60 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                      smem_u32(bar))
                  : "memory");
+}
+
+// --- CTA pair (cluster of 2) helpers ---
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t num_clusters_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared::cluster address of the same shared variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Completion of this thread's pair MMAs arrives on the barrier at a
+// shared::cluster address (either CTA of the pair).
+__device__ __forceinline__ void umma_commit_pair(uint32_t cluster_bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
+                 : "memory");
+}
+// Pair TMA load into this CTA's shared memory, completing on the barrier at
+// a shared::cluster address (the pair leader's).
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, int x, int y,
+                                                uint32_t cluster_bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(cluster_bar)
+        : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -136,8 +210,8 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + __expf(-g)); }
 
 struct FfnSmem {
-    uint64_t full[kStages];
-    uint64_t empty[kStages];
+    uint64_t full[kMaxStages];
+    uint64_t empty[kMaxStages];
     uint64_t tmem_full[2];
     uint64_t tmem_empty[2];
     uint32_t tmem_base;
@@ -162,6 +236,40 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
     }
 }
 
+// Epilogue staging: each epilogue warp owns 32 rows x 128 bytes (64 16-bit
+// columns) of shared memory.  Lane r writes its accumulator row r; the 16-byte
+// chunk j of row r sits at slot j ^ (r & 7), so that both the row-wise writes
+// (8 lanes cover all 32 banks) and the chunk-wise reads are conflict-free.
+constexpr uint32_t kWarpStageBytes = 32 * 128;
+constexpr uint32_t kStageBytes = 4 * kWarpStageBytes;
+
+__device__ __forceinline__ void stage_put(unsigned char* stg, int row, int chunk, const uint4& v) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(stg + row * 128 + ((chunk ^ (row & 7)) << 4))),
+                 "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// Writes the warp's staged 32 x 64 columns to dst rows 0..nrows-1 (columns
+// col0 .. col0+63, clipped at n_out): 4 rows x 128 contiguous bytes per warp
+// store instruction instead of 32 scattered 16-byte pieces.
+__device__ __forceinline__ void stage_flush(const unsigned char* stg, int lane, uint16_t* dst, int64_t stride,
+                                            int nrows, int col0, int n_out) {
+    __syncwarp();
+    const int ch = lane & 7;
+    const bool col_ok = col0 + ch * 8 < n_out;
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+        const int r = it * 4 + (lane >> 3);
+        uint4 v;
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "r"(smem_u32(stg + r * 128 + ((ch ^ (r & 7)) << 4)))
+                     : "memory");
+        if (r < nrows && col_ok) st_v4(reinterpret_cast<uint4*>(dst + int64_t(r) * stride + col0) + ch, v);
+    }
+    __syncwarp();
+}
+
 // Maps a linear 128-row block index to (segment, block within segment).
 __device__ __forceinline__ int find_segment(const int32_t* blk_prefix, int nseg, int g) {
     int lo = 0, hi = nseg - 1;
@@ -176,7 +284,7 @@ __device__ __forceinline__ int find_segment(const int32_t* blk_prefix, int nseg,
 // EPI = kEpiSwiGLU: B rows of N block n are gate rows [n*128, n*128+128) and up
 // rows [I + n*128, ...) of the expert; the output has n_out = I columns.
 // EPI = kEpiStore: B rows [n*256, n*256+256) of the expert; n_out columns.
-template <int EPI, int DT>
+template <int EPI, int DT, int CG>
 __global__ void __launch_bounds__(kFfnThreads, 1)
 grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     const int32_t* __restrict__ seg_start, const int32_t* __restrict__ seg_expert,
@@ -189,22 +297,31 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     // 1024-byte aligned stage buffers (SW128 atoms), control block after them.
     unsigned char* base = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    using GEO = Geo<CG>;
+    constexpr int kStages = GEO::kStages;
+    constexpr uint32_t kBBytes = GEO::kBBytes;
+    constexpr int kBlockRows = GEO::kBlockRows;
     unsigned char* sA = base;
     unsigned char* sB = base + kStages * kABytes;
-    FfnSmem* ctl = reinterpret_cast<FfnSmem*>(sB + kStages * kBBytes);
+    unsigned char* s_stage = sB + kStages * kBBytes;            // epilogue staging, kStageBytes
+    FfnSmem* ctl = reinterpret_cast<FfnSmem*>(s_stage + kStageBytes);
     int32_t* blk_prefix = reinterpret_cast<int32_t*>(ctl + 1);  // [nseg + 1]
     int32_t* s_start = blk_prefix + (nseg + 1);                 // [nseg + 1] row offsets
-    int32_t* s_expert = s_start + (nseg + 1);                   // [nseg] expert of each segment
-    // scatter mode (dst_base != nullptr): row r of segment s is stored at
+    // [nseg] expert of each segment (low 16 bits) | source rank << 16.  In
+    // scatter mode (dst_base != nullptr) row r of segment s is stored at
     // dst_base[seg_src[s]] + (seg_dst_row[s] + r) rows -- e.g. the back buffer
     // of the rank that sent the segment's rows
-    int32_t* s_src = s_expert + nseg;                           // [nseg]
-    int32_t* s_dst_row = s_src + nseg;                          // [nseg]
+    int32_t* s_expsrc = s_start + (nseg + 1);
+    int32_t* s_dst_row = s_expsrc + nseg;                       // [nseg]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     volatile int* abort_flag = &ctl->abort_flag;
     const int G = seg_groups > 1 ? seg_groups : 1;
     const int Lg = nseg / G;
+    // CTA-pair coordinates (CG = 2): rank 0 is the leader that issues the MMAs.
+    const uint32_t crank = CG == 2 ? cluster_rank() : 0u;
+    const int tile0 = CG == 2 ? int(cluster_id_x()) : int(blockIdx.x);
+    const int tile_step = CG == 2 ? int(num_clusters_x()) : int(gridDim.x);
 
     // Set-up: barriers, block prefix over segments, TMEM.
     if (threadIdx.x == 0) {
@@ -214,7 +331,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&ctl->tmem_full[b], 1);
-            mbar_init(&ctl->tmem_empty[b], 4);
+            mbar_init(&ctl->tmem_empty[b], 4 * CG);  // epilogue warps of every CTA of the group
         }
         ctl->abort_flag = 0;
         mbar_fence_init();
@@ -233,14 +350,11 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             if (i < nseg) {
                 const int lo = seg_start[i];
                 s_start[i] = lo;
-                s_expert[i] = seg_expert ? seg_expert[i] : i;
-                if (dst_base) {
-                    s_src[i] = seg_src[i];
-                    s_dst_row[i] = seg_dst_row[i];
-                }
+                s_expsrc[i] = (seg_expert ? seg_expert[i] : i) | (dst_base ? seg_src[i] << 16 : 0);
+                if (dst_base) s_dst_row[i] = seg_dst_row[i];
                 const int nat = G > 1 ? (i % G) * Lg + i / G : i;  // segment at tile-order position i
                 const int rows = seg_start[nat + 1] - seg_start[nat];
-                cnt = rows > 0 ? (rows + kTileM - 1) / kTileM : 0;
+                cnt = rows > 0 ? (rows + kBlockRows - 1) / kBlockRows : 0;
             }
             int incl = cnt;
 #pragma unroll
@@ -262,55 +376,77 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         }
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                         smem_u32(&ctl->tmem_base)),
-                     "r"(kTmemCols)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        if (CG == 1) {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32(&ctl->tmem_base)),
+                         "r"(kTmemCols)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32(&ctl->tmem_base)),
+                         "r"(kTmemCols)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if (CG == 2) cluster_sync();  // both CTAs' barriers initialised before any cross-CTA signal
     tc_fence_after();
 
     const uint32_t tmem = ctl->tmem_base;
     const int total_tiles = ctl->total_blocks * n_blocks;
     const int nk = (kdim + kTileK - 1) / kTileK;
+    const uint32_t leader_full0 = CG == 2 ? map_to_rank(&ctl->full[0], 0) : 0u;
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             uint32_t it = 0;
-            for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
+            for (int tile = tile0; tile < total_tiles && !*abort_flag; tile += tile_step) {
                 const int g = tile / n_blocks, n = tile % n_blocks;
                 const int ti = find_segment(blk_prefix, nseg, g);
                 const int s = G > 1 ? (ti % G) * Lg + ti / G : ti;
-                const int e = s_expert[s];
-                const int row0 = s_start[s] + (g - blk_prefix[ti]) * kTileM;
+                const int e = s_expsrc[s] & 0xffff;
+                const int row0 = s_start[s] + (g - blk_prefix[ti]) * kBlockRows + int(crank) * kTileM;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const int st = int(it % kStages);
                     if (!wait_or_abort(&ctl->empty[st], ((it / kStages) & 1u) ^ 1u, abort_flag, dev_status))
                         break;
-                    mbar_arrive_expect_tx(&ctl->full[st], kABytes + kBBytes);
-                    tma_load_2d(sA + st * kABytes, &tmap_a, kb * kTileK, row0, &ctl->full[st]);
                     unsigned char* b = sB + st * kBBytes;
-                    if (EPI == kEpiSwiGLU) {
-                        const int brow = e * b_rows_per_expert + n * (kTileN / 2);
-                        tma_load_2d(b, &tmap_b, kb * kTileK, brow, &ctl->full[st]);
-                        tma_load_2d(b + kBBytes / 2, &tmap_b, kb * kTileK, brow + gate_up_split,
-                                    &ctl->full[st]);
+                    if (CG == 1) {
+                        mbar_arrive_expect_tx(&ctl->full[st], kABytes + kBBytes);
+                        tma_load_2d(sA + st * kABytes, &tmap_a, kb * kTileK, row0, &ctl->full[st]);
+                        if (EPI == kEpiSwiGLU) {
+                            const int brow = e * b_rows_per_expert + n * (kTileN / 2);
+                            tma_load_2d(b, &tmap_b, kb * kTileK, brow, &ctl->full[st]);
+                            tma_load_2d(b + kBBytes / 2, &tmap_b, kb * kTileK, brow + gate_up_split,
+                                        &ctl->full[st]);
+                        } else {
+                            tma_load_2d(b, &tmap_b, kb * kTileK, e * b_rows_per_expert + n * kTileN,
+                                        &ctl->full[st]);
+                        }
                     } else {
-                        tma_load_2d(b, &tmap_b, kb * kTileK, e * b_rows_per_expert + n * kTileN,
-                                    &ctl->full[st]);
+                        // Both CTAs load their halves; the bytes land on the leader's barrier,
+                        // which the leader arms with the pair's total.
+                        const uint32_t fbar = leader_full0 + uint32_t(st) * 8u;
+                        if (crank == 0) mbar_arrive_expect_tx(&ctl->full[st], 2 * (kABytes + kBBytes));
+                        tma_load_2d_pair(sA + st * kABytes, &tmap_a, kb * kTileK, row0, fbar);
+                        const int brow = EPI == kEpiSwiGLU
+                                             ? e * b_rows_per_expert + n * (kTileN / 2) + int(crank) * gate_up_split
+                                             : e * b_rows_per_expert + n * kTileN + int(crank) * (kTileN / 2);
+                        tma_load_2d_pair(b, &tmap_b, kb * kTileK, brow, fbar);
                     }
                 }
             }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            const uint32_t idesc = umma_idesc(DT == MOE_B200_BF16 ? 1 : 0);
+        // ---------------- MMA issuer (the pair leader for CG = 2) ----------------
+        if (lane == 0 && crank == 0) {
+            const uint32_t idesc = umma_idesc(DT == MOE_B200_BF16 ? 1 : 0, kBlockRows);
             uint32_t it = 0, j = 0;
-            for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x, ++j) {
+            for (int tile = tile0; tile < total_tiles && !*abort_flag; tile += tile_step, ++j) {
                 const int buf = int(j & 1u);
                 if (!wait_or_abort(&ctl->tmem_empty[buf], ((j >> 1) & 1u) ^ 1u, abort_flag, dev_status))
                     break;
@@ -329,21 +465,34 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
 #pragma unroll
                     for (int kk = 0; kk < kTileK / 16; ++kk) {
                         // +32 bytes per 16-element K step inside the 128-byte swizzle row
-                        umma_f16(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32),
-                                 idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                        const uint64_t ad = umma_desc_sw128(a_addr + kk * 32), bd = umma_desc_sw128(b_addr + kk * 32);
+                        const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+                        if (CG == 1) umma_f16(d_tmem, ad, bd, idesc, acc);
+                        else umma_f16_pair(d_tmem, ad, bd, idesc, acc);
                     }
-                    umma_commit(&ctl->empty[st]);
+                    if (CG == 1) {
+                        umma_commit(&ctl->empty[st]);
+                    } else {  // free the stage in both CTAs
+                        umma_commit_pair(map_to_rank(&ctl->empty[st], 0));
+                        umma_commit_pair(map_to_rank(&ctl->empty[st], 1));
+                    }
                 }
                 if (!ok) break;
-                umma_commit(&ctl->tmem_full[buf]);
+                if (CG == 1) {
+                    umma_commit(&ctl->tmem_full[buf]);
+                } else {
+                    umma_commit_pair(map_to_rank(&ctl->tmem_full[buf], 0));
+                    umma_commit_pair(map_to_rank(&ctl->tmem_full[buf], 1));
+                }
             }
         }
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
         const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
-        const int r_in_tile = quad * 32 + lane;
+        unsigned char* stg = s_stage + quad * kWarpStageBytes;
         uint32_t j = 0;
-        for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++j) {
+        const uint32_t leader_tmem_empty0 = CG == 2 ? map_to_rank(&ctl->tmem_empty[0], 0) : 0u;
+        for (int tile = tile0; tile < total_tiles; tile += tile_step, ++j) {
             const int buf = int(j & 1u);
             if (!wait_or_abort(&ctl->tmem_full[buf], (j >> 1) & 1u, abort_flag, dev_status)) break;
             tc_fence_after();
@@ -352,12 +501,19 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             const int s = G > 1 ? (ti % G) * Lg + ti / G : ti;
             const int blk = g - blk_prefix[ti];
             const int seg_rows = s_start[s + 1] - s_start[s];
-            const bool row_ok = blk * kTileM + r_in_tile < seg_rows;
-            const int64_t row = int64_t(s_start[s]) + blk * kTileM + r_in_tile;
-            uint16_t* out_row = out + row * out_stride;
+            // This warp's 32 rows start at segment row w_row0; nrows_w of them are in the segment.
+            const int w_row0 = blk * kBlockRows + int(crank) * kTileM + quad * 32;
+            const int nrows_w = seg_rows - w_row0;
+            // Row 0 of the segment at its destination: the local output, or
+            // in scatter mode the sender's buffer on the rank that sent it.
+            uint16_t* dst0 = dst_base ? reinterpret_cast<uint16_t*>(dst_base[s_expsrc[s] >> 16]) +
+                                            int64_t(s_dst_row[s]) * out_stride
+                                      : out + int64_t(s_start[s]) * out_stride;
+            dst0 += int64_t(w_row0) * out_stride;
             const uint32_t t_row = tmem + uint32_t(buf) * kTileN + (uint32_t(quad * 32) << 16);
             if (EPI == kEpiSwiGLU) {
-                // 32 gate + 32 up columns per TMEM round trip
+                // 32 gate + 32 up columns per TMEM round trip; every second
+                // round flushes 64 output columns from the staging tile.
 #pragma unroll 1
                 for (int c = 0; c < kTileN / 2; c += 32) {
                     uint32_t gr[2][16], ur[2][16];
@@ -368,20 +524,18 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                     tmem_wait_ld();
 #pragma unroll
                     for (int hb = 0; hb < 2; ++hb) {
-                        const int col = n * (kTileN / 2) + c + hb * 16;
-                        if (row_ok && col < n_out) {
-                            uint32_t o[8];
+                        uint32_t o[8];
 #pragma unroll
-                            for (int q = 0; q < 8; ++q) {
-                                const float g0 = __uint_as_float(gr[hb][2 * q]), g1 = __uint_as_float(gr[hb][2 * q + 1]);
-                                const float u0 = __uint_as_float(ur[hb][2 * q]), u1 = __uint_as_float(ur[hb][2 * q + 1]);
-                                o[q] = pack2<DT>(silu(g0) * u0, silu(g1) * u1);
-                            }
-                            uint4* dst = reinterpret_cast<uint4*>(out_row + col);
-                            st_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
-                            st_v4(dst + 1, make_uint4(o[4], o[5], o[6], o[7]));
+                        for (int q = 0; q < 8; ++q) {
+                            const float g0 = __uint_as_float(gr[hb][2 * q]), g1 = __uint_as_float(gr[hb][2 * q + 1]);
+                            const float u0 = __uint_as_float(ur[hb][2 * q]), u1 = __uint_as_float(ur[hb][2 * q + 1]);
+                            o[q] = pack2<DT>(silu(g0) * u0, silu(g1) * u1);
                         }
+                        const int ch = ((c & 32) >> 3) + 2 * hb;  // 16-byte chunk of the 64-column staging row
+                        stage_put(stg, lane, ch, make_uint4(o[0], o[1], o[2], o[3]));
+                        stage_put(stg, lane, ch + 1, make_uint4(o[4], o[5], o[6], o[7]));
                     }
+                    if (c & 32) stage_flush(stg, lane, dst0, out_stride, nrows_w, n * (kTileN / 2) + c - 32, n_out);
                 }
             } else {
                 // 64 columns per TMEM round trip
@@ -393,40 +547,22 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                     tmem_wait_ld();
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
-                        const int col = n * kTileN + c + 16 * q4;
-                        if (row_ok && col < n_out) {
-                            uint32_t o[8];
+                        uint32_t o[8];
 #pragma unroll
-                            for (int q = 0; q < 8; ++q)
-                                o[q] = pack2<DT>(__uint_as_float(v[q4][2 * q]), __uint_as_float(v[q4][2 * q + 1]));
-                            uint4* dst = reinterpret_cast<uint4*>(out_row + col);
-                            st_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
-                            st_v4(dst + 1, make_uint4(o[4], o[5], o[6], o[7]));
-                        }
+                        for (int q = 0; q < 8; ++q)
+                            o[q] = pack2<DT>(__uint_as_float(v[q4][2 * q]), __uint_as_float(v[q4][2 * q + 1]));
+                        stage_put(stg, lane, 2 * q4, make_uint4(o[0], o[1], o[2], o[3]));
+                        stage_put(stg, lane, 2 * q4 + 1, make_uint4(o[4], o[5], o[6], o[7]));
                     }
-                }
-                if (dst_base) {
-                    // Forward this warp's 32 finished rows (this tile's columns)
-                    // to their destinations, one whole row slice per warp store
-                    // (lane = 16-byte chunk): coalesced writes over NVLink.
-                    __syncwarp();
-                    const int c0 = n * kTileN;
-                    const int ncol = n_out - c0 < kTileN ? n_out - c0 : kTileN;
-                    const int nchunk = ncol / 8;
-                    const int64_t seg_row0 = int64_t(blk) * kTileM + quad * 32;
-                    uint16_t* dbase = reinterpret_cast<uint16_t*>(dst_base[s_src[s]]);
-                    for (int rr = 0; rr < 32; ++rr) {
-                        if (seg_row0 + rr >= seg_rows) break;
-                        const uint16_t* src = out + (int64_t(s_start[s]) + seg_row0 + rr) * out_stride + c0;
-                        uint16_t* dst = dbase + (int64_t(s_dst_row[s]) + seg_row0 + rr) * out_stride + c0;
-                        for (int ch = lane; ch < nchunk; ch += 32)
-                            st_v4(reinterpret_cast<uint4*>(dst) + ch, __ldcg(reinterpret_cast<const uint4*>(src) + ch));
-                    }
+                    stage_flush(stg, lane, dst0, out_stride, nrows_w, n * kTileN + c, n_out);
                 }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&ctl->tmem_empty[buf]);
+            if (lane == 0) {
+                if (CG == 1) mbar_arrive(&ctl->tmem_empty[buf]);
+                else mbar_arrive_cluster(leader_tmem_empty0 + uint32_t(buf) * 8u);
+            }
         }
     }
 
@@ -435,11 +571,16 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     if (dst_base && warp >= 2) __threadfence_system();
     tc_fence_before();
     __syncthreads();
+    if (CG == 2) cluster_sync();  // no CTA leaves while its pair may still signal it
     tc_fence_after();
     if (warp == 1) {
         __syncwarp();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
-                     : "memory");
+        if (CG == 1)
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+                         : "memory");
+        else
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+                         : "memory");
     }
 }
 
@@ -479,8 +620,10 @@ static bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t c
     return r == CUDA_SUCCESS;
 }
 
+template <int CG>
 static size_t ffn_smem_bytes(int nseg) {
-    return 1024 + kStages * (kABytes + kBBytes) + sizeof(FfnSmem) + size_t(5 * nseg + 2) * 4;
+    return 1024 + Geo<CG>::kStages * (kABytes + Geo<CG>::kBBytes) + kStageBytes + sizeof(FfnSmem) +
+           size_t(4 * nseg + 2) * 4;
 }
 
 static int sm_count_ffn() {
@@ -489,25 +632,72 @@ static int sm_count_ffn() {
     return n > 0 ? n : 148;
 }
 
-template <int EPI, int DT>
+// CTA groups of the two GEMMs, bit 0: gate/up GEMM on SM pairs, bit 1: down
+// GEMM on SM pairs.  MOE_B200_FFN=1sm / 2sm forces one form for both; the
+// default runs the gate/up GEMM on single SMs and the down GEMM (whose
+// epilogue stores twice the columns per MMA step) on SM pairs when the
+// segments average at least 512 rows, so that 256-row tiles waste little.
+static int ffn_cta_groups(int rows, int nseg) {
+    const char* v = std::getenv("MOE_B200_FFN");
+    if (v && std::strcmp(v, "1sm") == 0) return 0;
+    if (v && std::strcmp(v, "2sm") == 0) return 3;
+    return rows >= 512 * nseg ? 2 : 0;
+}
+
+template <int EPI, int DT, int CG>
 static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb_, const int32_t* seg_start,
                                const int32_t* seg_expert, int nseg, int rows, int kdim, int b_rows_per_expert,
                                int n_out, int n_blocks, int split, void* out, int64_t out_stride,
                                uint32_t* st, cudaStream_t stream, char* const* dst_base = nullptr,
                                const int32_t* seg_src = nullptr, const int32_t* seg_dst_row = nullptr,
                                int seg_groups = 1) {
-    const size_t smem = ffn_smem_bytes(nseg);
-    auto kern = grouped_gemm_kernel<EPI, DT>;
+    const size_t smem = ffn_smem_bytes<CG>(nseg);
+    auto kern = grouped_gemm_kernel<EPI, DT, CG>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (err != cudaSuccess) return err;
     // Upper bound on tiles: every segment may add one partial block.
-    const int64_t max_tiles = (int64_t(rows) / kTileM + nseg) * n_blocks;
-    int grid = sm_count_ffn();
-    if (max_tiles < grid) grid = int(max_tiles > 0 ? max_tiles : 1);
-    cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(kFfnThreads), smem, stream);
+    const int64_t max_tiles = (int64_t(rows) / Geo<CG>::kBlockRows + nseg) * n_blocks;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_config(dim3(1), dim3(kFfnThreads), smem, stream);
+    int groups = sm_count_ffn() / CG;
+    if (CG == 2) {
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cfg.gridDim = dim3(2 * groups);
+        int active = 0;
+        if (cudaOccupancyMaxActiveClusters(&active, kern, &cfg) == cudaSuccess && active > 0 && active < groups)
+            groups = active;
+        cudaGetLastError();
+    }
+    if (max_tiles < groups) groups = int(max_tiles > 0 ? max_tiles : 1);
+    cfg.gridDim = dim3(CG * groups);
     return cudaLaunchKernelEx(&cfg, kern, ma, mb_, seg_start, seg_expert, nseg, kdim, b_rows_per_expert, n_out,
                               n_blocks, split, static_cast<uint16_t*>(out), out_stride, st, dst_base, seg_src,
                               seg_dst_row, seg_groups);
+}
+
+template <int DT>
+static cudaError_t launch_ffn(int cg, const CUtensorMap& mx, const CUtensorMap& mwgu, const CUtensorMap& mh,
+                              const CUtensorMap& mwd, const int32_t* seg_start, const int32_t* seg_expert, int nseg,
+                              int rows, int d, int I, void* h, void* y, uint32_t* st, cudaStream_t s,
+                              char* const* dst_base, const int32_t* seg_src, const int32_t* seg_dst_row,
+                              int seg_groups) {
+    const int nb1 = (I + kTileN / 2 - 1) / (kTileN / 2);
+    const int nb2 = (d + kTileN - 1) / kTileN;
+    cudaError_t err =
+        (cg & 1) ? launch_gemm<kEpiSwiGLU, DT, 2>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1, I, h,
+                                                  I, st, s, nullptr, nullptr, nullptr, seg_groups)
+                 : launch_gemm<kEpiSwiGLU, DT, 1>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1, I, h,
+                                                  I, st, s, nullptr, nullptr, nullptr, seg_groups);
+    if (err != cudaSuccess) return err;
+    return (cg & 2) ? launch_gemm<kEpiStore, DT, 2>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0, y, d,
+                                                    st, s, dst_base, seg_src, seg_dst_row, seg_groups)
+                    : launch_gemm<kEpiStore, DT, 1>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0, y, d,
+                                                    st, s, dst_base, seg_src, seg_dst_row, seg_groups);
 }
 
 int fail(int code, const char* fmt, ...);
@@ -539,28 +729,21 @@ int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* 
     if (rows == 0) return MOE_B200_OK;
     uint32_t* st = device_status_word();
     if (!st) return fail(MOE_B200_ERR_CUDA, "grouped_swiglu: device status word unavailable");
+    const int cg = ffn_cta_groups(rows, nseg);
     CUtensorMap mx, mwgu, mh, mwd;
+    // A boxes hold one CTA's 128 rows; each CTA of a pair holds half of the
+    // 256 B rows of a down-projection tile.
     if (!make_map(&mx, x, rows, d, kTileM, dtype) ||
         !make_map(&mwgu, w_gate_up, int64_t(E) * 2 * I, d, kTileN / 2, dtype) ||
         !make_map(&mh, h, rows, I, kTileM, dtype) ||
-        !make_map(&mwd, w_down, int64_t(E) * d, I, kTileN, dtype))
+        !make_map(&mwd, w_down, int64_t(E) * d, I, (cg & 2) ? kTileN / 2 : kTileN, dtype))
         return fail(MOE_B200_ERR_CUDA, "grouped_swiglu: cuTensorMapEncodeTiled failed");
-    const int nb1 = (I + kTileN / 2 - 1) / (kTileN / 2);
-    const int nb2 = (d + kTileN - 1) / kTileN;
-    cudaError_t err;
-    if (dtype == MOE_B200_BF16) {
-        err = launch_gemm<kEpiSwiGLU, MOE_B200_BF16>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1,
-                                                     I, h, I, st, s, nullptr, nullptr, nullptr, seg_groups);
-        if (err == cudaSuccess)
-            err = launch_gemm<kEpiStore, MOE_B200_BF16>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0,
-                                                        y, d, st, s, dst_base, seg_src, seg_dst_row, seg_groups);
-    } else {
-        err = launch_gemm<kEpiSwiGLU, MOE_B200_F16>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1,
-                                                    I, h, I, st, s, nullptr, nullptr, nullptr, seg_groups);
-        if (err == cudaSuccess)
-            err = launch_gemm<kEpiStore, MOE_B200_F16>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0,
-                                                       y, d, st, s, dst_base, seg_src, seg_dst_row, seg_groups);
-    }
+    const cudaError_t err =
+        dtype == MOE_B200_BF16
+            ? launch_ffn<MOE_B200_BF16>(cg, mx, mwgu, mh, mwd, seg_start, seg_expert, nseg, rows, d, I, h, y, st, s,
+                                        dst_base, seg_src, seg_dst_row, seg_groups)
+            : launch_ffn<MOE_B200_F16>(cg, mx, mwgu, mh, mwd, seg_start, seg_expert, nseg, rows, d, I, h, y, st, s,
+                                       dst_base, seg_src, seg_dst_row, seg_groups);
     return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "grouped_swiglu launch");
 }
 }  // namespace moe_b200
