@@ -34,6 +34,7 @@ ERR_UNSUPPORTED = 3
 ERR_CUDA = 4
 DEV_BAD_ASSIGNMENT = 0x10
 DEV_WAIT_TIMEOUT = 0x20
+DEV_BAD_WEIGHTS = 0x40
 F16 = 0
 BF16 = 1
 MAX_EXPERTS = 1024
@@ -76,6 +77,12 @@ def lib() -> ctypes.CDLL:
     L.moe_b200_device_status.argtypes = [vp, ctypes.POINTER(cint)]
     L.moe_b200_grouped_swiglu.restype = cint
     L.moe_b200_grouped_swiglu.argtypes = [vp, vp, vp, cint, cint, cint, cint, cint, vp, vp, cint, vp, vp, vp]
+    L.moe_b200_router_weights_bytes.restype = sz
+    L.moe_b200_router_weights_bytes.argtypes = [cint, cint, cint]
+    L.moe_b200_router_prepare.restype = cint
+    L.moe_b200_router_prepare.argtypes = [vp, cint, cint, cint, vp, vp]
+    L.moe_b200_route.restype = cint
+    L.moe_b200_route.argtypes = [vp, cint, cint, cint, cint, cint, vp, vp, vp, vp]
     L.moe_b200_ep_layout.restype = cint
     L.moe_b200_ep_layout.argtypes = [vp, cint, cint, cint, ctypes.POINTER(ctypes.c_int32), vp, vp, vp, vp, vp]
     u64 = ctypes.c_uint64
@@ -334,6 +341,40 @@ def grouped_swiglu(x, seg_start, w_gate_up, w_down, seg_expert=None, h=None, y=N
                                          _ptr(w_gate_up), _ptr(w_down), dtype_code(x.dtype), _ptr(h), _ptr(y),
                                          _stream_handle(stream)), "grouped_swiglu")
     return h, y
+
+
+class RouterWeights:
+    """Gate weights prepared for moe_b200_route: w_gate [d, E] fp32 on the
+    device (row i = input feature i, as the reference's W_gate), split into
+    16-bit pieces of the embeddings' dtype and transposed once."""
+
+    def __init__(self, w_gate, dtype, stream=None):
+        import torch
+        if w_gate.dtype != torch.float32 or w_gate.dim() != 2:
+            raise MoEB200Error(ERR_INVALID_ARG, "RouterWeights: w_gate must be a 2-D float32 tensor [d, E]")
+        self.d, self.E = w_gate.shape
+        self.dtype = dtype
+        nbytes = lib().moe_b200_router_weights_bytes(self.d, self.E, dtype_code(dtype))
+        if nbytes == 0:
+            raise MoEB200Error(ERR_INVALID_ARG, f"RouterWeights: bad shape d={self.d} E={self.E}")
+        self.buf = torch.empty(nbytes, dtype=torch.uint8, device=w_gate.device)
+        _check(lib().moe_b200_router_prepare(_ptr(w_gate.contiguous()), self.d, self.E, dtype_code(dtype),
+                                             _ptr(self.buf), _stream_handle(stream)), "router_prepare")
+
+
+def route(x, weights, K, out=None, stream=None):
+    """Router on the tensor cores: x [T, d] (bf16/fp16), weights a
+    RouterWeights of the same dtype.  Returns (assignments int32 [T, K],
+    routing weights fp32 [T, K]): the K most probable experts of the softmax
+    over all E logits, in descending probability, ties to the lower index."""
+    import torch
+    T, d = x.shape
+    if out is None:
+        out = (torch.empty((T, K), dtype=torch.int32, device=x.device),
+               torch.empty((T, K), dtype=torch.float32, device=x.device))
+    _check(lib().moe_b200_route(_ptr(x), T, d, weights.E, K, dtype_code(x.dtype), _ptr(weights.buf),
+                                _ptr(out[0]), _ptr(out[1]), _stream_handle(stream)), "route")
+    return out
 
 
 def ep_layout(all_counts, rank, expert_first, out=None, stream=None):

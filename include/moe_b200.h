@@ -41,7 +41,8 @@ enum moe_b200_status {
     MOE_B200_ERR_CUDA = 4,             /* a CUDA call or launch failed */
     /* device-side conditions, reported by moe_b200_workspace_status() as bits */
     MOE_B200_DEV_BAD_ASSIGNMENT = 0x10, /* some assignment was outside [0, E) */
-    MOE_B200_DEV_WAIT_TIMEOUT = 0x20    /* a bounded cross-CTA wait gave up */
+    MOE_B200_DEV_WAIT_TIMEOUT = 0x20,   /* a bounded cross-CTA wait gave up */
+    MOE_B200_DEV_BAD_WEIGHTS = 0x40     /* router weights not prepared for this d / E / dtype */
 };
 
 enum moe_b200_dtype { MOE_B200_F16 = 0, MOE_B200_BF16 = 1 };
@@ -139,6 +140,33 @@ int moe_b200_device_status(void* stream, int* device_status /* host */);
  *   y [T*K, d] 16-bit expert outputs in packed order; out [T, d] 16-bit.    */
 int moe_b200_unpermute(const void* y, const float* packed_weights, const int32_t* slot_pos,
                        int T, int K, int d, int dtype, void* out, void* stream);
+
+/* -------------------------------------------------------------- router ---- */
+
+/* Router: gate GEMM + softmax over all E experts + top-K, one kernel on the
+ * tcgen05 tensor cores with the logits kept on chip:
+ *   logit[t, e] = sum_i emb[t, i] * w_gate[i, e]               (fp32)
+ *   p[t, e]     = expf(logit - max_e logit) / sum_e expf(...)  (ascending e)
+ *   assignments[t, k], weights[t, k] = the K largest p[t, :] in descending
+ *   order, ties to the lower expert index; weights are the softmax
+ *   probabilities themselves (not renormalised over K).
+ * Replaces fused_route_kernel (apps/bench_e2e.cu:95-130) and the unfused
+ * gate_kernel / softmax_kernel / topk_kernel chain (apps/bench_e2e.cu:51-93),
+ * same argument meaning (w_gate [d, E] fp32, row i = input feature i).
+ *
+ * The fp32 gate weights are prepared once (moe_b200_router_prepare) into a
+ * caller-allocated buffer of moe_b200_router_weights_bytes(d, E, dtype)
+ * bytes: transposed to K-major and split into 16-bit pieces of the
+ * embeddings' type whose sum is w_gate to 22 (fp16, 2 pieces, power-of-two
+ * pre-scaled) or 24 (bf16, 3 pieces) significant bits, so the tensor cores
+ * take the embeddings unconverted and the logits keep fp32 accuracy.
+ * Limits: d a multiple of 8; 1 <= E <= 256 (fp16) or 128 (bf16);
+ * 1 <= K <= min(8, E).  Pointers 16-byte aligned.                           */
+size_t moe_b200_router_weights_bytes(int d, int E, int dtype);
+int moe_b200_router_prepare(const float* w_gate, int d, int E, int dtype, void* packed_weights,
+                            void* stream);
+int moe_b200_route(const void* emb, int T, int d, int E, int K, int dtype, const void* packed_weights,
+                   int32_t* assignments, float* weights, void* stream);
 
 /* ---------------------------------------------------------- expert FFN ---- */
 

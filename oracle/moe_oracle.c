@@ -12,11 +12,13 @@
  * reference's shipped fixtures (results/syn_{uniform,zipf}_T{512,2048,8192})
  * and on the verify.cu mini test (apps/verify.cu:114-128).
  *
- * oracle_combine() and oracle_swiglu_expert() have no counterpart in the
- * reference's CPU code (the reference combines only on the GPU with fp32
- * atomics, apps/bench_e2e.cu:136-152, and its FFN has no activation,
- * apps/bench_e2e.cu:289-299): their parity is "unpinned" and rests on the
- * closed-form identity-expert case and on torch fp32 cross-checks.
+ * oracle_combine(), oracle_swiglu_expert() and oracle_route() have no
+ * counterpart in the reference's CPU code (the reference combines only on the
+ * GPU with fp32 atomics, apps/bench_e2e.cu:136-152, its FFN has no
+ * activation, apps/bench_e2e.cu:289-299, and it routes only on the GPU,
+ * apps/bench_e2e.cu:51-130): their parity is "unpinned" and rests on the
+ * closed-form identity-expert case, torch fp32 cross-checks and, for the
+ * router, a restatement of the reference kernel's float arithmetic (mode 0).
  *
  * All 16-bit payloads are opaque uint16 words; dtype 0 = fp16, 1 = bf16.
  */
@@ -286,4 +288,84 @@ void oracle_swiglu_expert(const uint16_t* x, const uint16_t* w_gu, const uint16_
         }
     }
     free(xf); free(hf); free(wrow); free(gacc); free(uacc);
+}
+
+/* ------------------------------------------------------------------------ */
+/* Router: gate GEMM + softmax over all E + top-K (apps/bench_e2e.cu:95-130,
+ * fused_route_kernel; the unfused gate/softmax/topk kernels :51-93 compute
+ * the same).  emb [T, d] 16-bit, w_gate [d, E] fp32 (row i = input feature).
+ *   mode 0: the reference's own arithmetic -- logit accumulated in float in
+ *           ascending i as fmaf(x_i, W[i*E+e], logit) (nvcc contracts the
+ *           reference's `logit += a * b` into a fused multiply-add), max,
+ *           expf(l - max) summed in ascending e, one division per expert,
+ *           K rounds of strict-greater argmax (ties to the lower index);
+ *   mode 1: logits and softmax in double, the order-independent target;
+ *           weights rounded to float at the end.
+ * margin[t] (may be NULL): p_K - p_{K+1} of the double computation (1 when
+ * K == E); a token with a tiny margin may legitimately select a different
+ * K-th expert under another summation order.                               */
+void oracle_route(const uint16_t* emb, const float* w_gate, int T, int d, int E, int K, int dtype, int mode,
+                  int32_t* asgn, float* wts, double* margin) {
+    float* x = (float*)malloc(sizeof(float) * (size_t)d);
+    float* pf = (float*)malloc(sizeof(float) * (size_t)E);
+    double* pd = (double*)malloc(sizeof(double) * (size_t)E);
+    for (int t = 0; t < T; ++t) {
+        for (int i = 0; i < d; ++i) x[i] = to_f32(emb[(size_t)t * d + i], dtype);
+        for (int e = 0; e < E; ++e) {
+            double ld = 0.0;
+            float lf = 0.f;
+            for (int i = 0; i < d; ++i) {
+                const float w = w_gate[(size_t)i * E + e];
+                ld += (double)x[i] * (double)w;
+                lf = fmaf(x[i], w, lf);
+            }
+            pd[e] = ld;
+            pf[e] = lf;
+        }
+        /* double softmax (also gives the margin) */
+        double mxd = pd[0];
+        for (int e = 1; e < E; ++e) if (pd[e] > mxd) mxd = pd[e];
+        double sd = 0.0;
+        for (int e = 0; e < E; ++e) { pd[e] = exp(pd[e] - mxd); sd += pd[e]; }
+        for (int e = 0; e < E; ++e) pd[e] /= sd;
+        /* float softmax, the reference's sequence */
+        float mxf = pf[0];
+        for (int e = 1; e < E; ++e) mxf = fmaxf(mxf, pf[e]);
+        float sf = 0.f;
+        for (int e = 0; e < E; ++e) { pf[e] = expf(pf[e] - mxf); sf += pf[e]; }
+        for (int e = 0; e < E; ++e) pf[e] /= sf;
+        double kth = 0.0;
+        for (int k = 0; k < K; ++k) {
+            int best = 0;
+            if (mode == 0) {
+                for (int e = 1; e < E; ++e) if (pf[e] > pf[best]) best = e;
+                asgn[(size_t)t * K + k] = best;
+                wts[(size_t)t * K + k] = pf[best];
+                pf[best] = -1.f;
+            } else {
+                for (int e = 1; e < E; ++e) if (pd[e] > pd[best]) best = e;
+                asgn[(size_t)t * K + k] = best;
+                wts[(size_t)t * K + k] = (float)pd[best];
+            }
+            if (mode != 0) { kth = pd[best]; pd[best] = -1.0; }
+        }
+        if (margin) {
+            if (mode == 0) {  /* recompute the double ranking for the margin */
+                double p1 = -1.0, p2 = -1.0;  /* K-th and (K+1)-th largest */
+                for (int k = 0; k <= K && k < E; ++k) {
+                    int best = 0;
+                    for (int e = 1; e < E; ++e) if (pd[e] > pd[best]) best = e;
+                    if (k == K - 1) p1 = pd[best];
+                    if (k == K) p2 = pd[best];
+                    pd[best] = -1.0;
+                }
+                margin[t] = K >= E ? 1.0 : p1 - p2;
+            } else {
+                double nxt = -1.0;
+                for (int e = 0; e < E; ++e) if (pd[e] > nxt) nxt = pd[e];
+                margin[t] = K >= E ? 1.0 : kth - nxt;
+            }
+        }
+    }
+    free(x); free(pf); free(pd);
 }

@@ -50,6 +50,7 @@ def lib():
         L.oracle_swiglu_expert.restype = None
         L.oracle_swiglu_expert.argtypes = [_P, _P, _P, _I, _I, _I, _I, _P, _P]
         L.oracle_f32_to_16_array.restype = None
+        L.oracle_route.argtypes = [_P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P]
         L.oracle_f32_to_16_array.argtypes = [_P, _P, _L, _I]
         L.oracle_16_to_f32_array.restype = None
         L.oracle_16_to_f32_array.argtypes = [_P, _P, _L, _I]
@@ -148,6 +149,21 @@ def swiglu_expert(x, w_gu, w_dn, dtype):
     y = np.empty((M, D), np.uint16)
     lib().oracle_swiglu_expert(_p(x), _p(w_gu), _p(w_dn), M, D, I, dtype, _p(h), _p(y))
     return h, y
+
+
+def route(emb, w_gate, K, dtype, mode=1):
+    """Router oracle: emb uint16 [T, d], w_gate float32 [d, E].  mode 0 = the
+    reference's float arithmetic, mode 1 = double.  Returns (assignments
+    int32 [T, K], weights float32 [T, K], margin float64 [T])."""
+    emb = _c(emb, np.uint16)
+    w_gate = _c(w_gate, np.float32)
+    T, d = emb.shape
+    E = w_gate.shape[1]
+    a = np.empty((T, K), np.int32)
+    w = np.empty((T, K), np.float32)
+    m = np.empty(T, np.float64)
+    lib().oracle_route(_p(emb), _p(w_gate), T, d, E, K, dtype, mode, _p(a), _p(w), _p(m))
+    return a, w, m
 
 
 def f32_to_16(a, dtype):

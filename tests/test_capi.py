@@ -92,3 +92,21 @@ def test_errors_raise():
     with pytest.raises(mb.MoEB200Error) as ei:
         mb._check(mb.ERR_WORKSPACE, "x")
     assert ei.value.status == mb.ERR_WORKSPACE
+
+
+def test_router_rejects_bad_arguments_on_host():
+    L = mb.lib()
+    p = 0x2000
+    assert L.moe_b200_router_weights_bytes(2048, 60, mb.F16) == 256 + 2 * 64 * 2048 * 2
+    assert L.moe_b200_router_weights_bytes(4096, 128, mb.BF16) == 256 + 3 * 128 * 4096 * 2
+    assert L.moe_b200_router_weights_bytes(0, 60, mb.F16) == 0
+    assert L.moe_b200_route(p, 16, 64, 16, 9, mb.F16, p, p, p, None) == mb.ERR_UNSUPPORTED   # K > 8
+    assert L.moe_b200_route(p, 16, 64, 4, 5, mb.F16, p, p, p, None) == mb.ERR_UNSUPPORTED    # K > E
+    assert L.moe_b200_route(p, 16, 60, 16, 2, mb.F16, p, p, p, None) == mb.ERR_UNSUPPORTED   # d % 8
+    assert L.moe_b200_route(p, 16, 64, 129, 2, mb.BF16, p, p, p, None) == mb.ERR_UNSUPPORTED  # E > 128 bf16
+    assert L.moe_b200_route(p, 16, 64, 16, 2, 7, p, p, p, None) == mb.ERR_INVALID_ARG        # dtype
+    assert L.moe_b200_route(p, -1, 64, 16, 2, mb.F16, p, p, p, None) == mb.ERR_INVALID_ARG
+    assert L.moe_b200_route(None, 16, 64, 16, 2, mb.F16, p, p, p, None) == mb.ERR_INVALID_ARG
+    assert L.moe_b200_route(p + 8, 16, 64, 16, 2, mb.F16, p, p, p, None) == mb.ERR_INVALID_ARG  # alignment
+    assert L.moe_b200_route(p, 0, 64, 16, 2, mb.F16, p, p, p, None) == mb.OK  # empty: no-op
+    assert L.moe_b200_router_prepare(None, 64, 16, mb.F16, p, None) == mb.ERR_INVALID_ARG

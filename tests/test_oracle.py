@@ -156,3 +156,42 @@ def test_swiglu_expert_vs_torch_fp32():
     yt = ht @ torch.from_numpy(oracle.to_f32(wdn, 1)).T
     np.testing.assert_allclose(oracle.to_f32(h, 1), ht.numpy(), rtol=2e-2, atol=2e-2)
     np.testing.assert_allclose(oracle.to_f32(y, 1), yt.numpy(), rtol=2e-2, atol=2e-2)
+
+
+def test_route_oracle_modes_agree_and_follow_reference_rules():
+    """oracle_route restates fused_route_kernel (apps/bench_e2e.cu:95-130):
+    softmax over all E, K rounds of strict-greater argmax.  The reference's
+    float arithmetic (mode 0) and the double computation (mode 1) pick the
+    same experts away from near-ties, and the weights are probabilities."""
+    rng = np.random.default_rng(0)
+    T, d, E, K = 300, 96, 20, 4
+    emb = oracle.f32_to_16(rng.standard_normal((T, d)).astype(np.float32), 0)
+    w = rng.uniform(-0.05, 0.05, size=(d, E)).astype(np.float32)
+    a0, p0, m = oracle.route(emb, w, K, 0, mode=0)
+    a1, p1, _ = oracle.route(emb, w, K, 0, mode=1)
+    ok = m > 1e-6
+    assert ok.mean() > 0.99
+    assert np.array_equal(a0[ok], a1[ok])
+    np.testing.assert_allclose(p0, p1, rtol=1e-5, atol=1e-8)
+    assert np.all(np.diff(p1, axis=1) <= 0)          # descending
+    assert np.all(p1.sum(1) <= 1.0 + 1e-6)
+    for t in range(T):
+        assert len(set(a1[t])) == K                  # without replacement
+    # tie: identical columns -> identical probabilities, lower index first
+    w[:, 7] = w[:, 2]
+    a, _, _ = oracle.route(emb, w, E, 0, mode=0)
+    for t in range(T):
+        row = list(a[t])
+        assert row.index(2) < row.index(7)
+
+
+def test_route_oracle_hand_example():
+    """Two tokens, d = 1: logits are the weights times the embedding."""
+    emb = oracle.f32_to_16(np.array([[1.0], [-1.0]], np.float32), 0)
+    w = np.array([[0.5, -0.25, 0.125, 1.0]], np.float32)
+    a, p, _ = oracle.route(emb, w, 2, 0, mode=1)
+    l = np.array([[0.5, -0.25, 0.125, 1.0], [-0.5, 0.25, -0.125, -1.0]])
+    prob = np.exp(l - l.max(1, keepdims=True))
+    prob /= prob.sum(1, keepdims=True)
+    assert a.tolist() == [[3, 0], [1, 2]]
+    np.testing.assert_allclose(p, np.sort(prob, 1)[:, ::-1][:, :2], rtol=1e-6)
