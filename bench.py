@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                     help="N>1 expert placement: popularity dealt round-robin over ranks (default) or the "
                          "reference's contiguous ranges")
+    ap.add_argument("--no-router", action="store_true",
+                    help="skip the separate router timing (N=1 pack configs)")
     ap.add_argument("--ep", default="fused", choices=["fused", "nccl"],
                     help="N>1 exchange: fused peer-store kernels (default) or NCCL AllToAllv")
     return ap.parse_args()
@@ -308,6 +310,43 @@ def reference_arm(args):
 
 # ------------------------------------------------------------ GPU arm -----
 
+def router_leg(mb, c, emb, stream, dev, flusher, steps, warm):
+    """Times moe_b200_route on the workload's tokens: random gate weights
+    U(-0.05, 0.05) [d, E] fp32 (the reference's fill_random_float,
+    include/moe/fp16_host.hpp:32-39), L2 flushed before every launch."""
+    import torch
+    T, K, E, d = c["T"], c["K"], c["E"], c["d"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(42)
+    w_gate = (torch.rand((d, E), generator=g, device=dev) - 0.5) * 0.1
+    with torch.cuda.stream(stream):
+        rw = mb.RouterWeights(w_gate, emb.dtype, stream=stream)
+        out = (torch.empty((T, K), dtype=torch.int32, device=dev),
+               torch.empty((T, K), dtype=torch.float32, device=dev))
+        for i in range(warm):
+            flusher(i)
+            mb.route(emb, rw, K, out=out, stream=stream)
+        evs = []
+        for i in range(steps):
+            flusher(i)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            mb.route(emb, rw, K, out=out, stream=stream)
+            b.record(stream)
+            evs.append((a, b))
+        torch.cuda.synchronize(dev)
+    assert mb.device_status(stream) == 0, "device-side condition in the router"
+    us = statistics.median(a.elapsed_time(b) for a, b in evs) * 1e3
+    nbytes = T * d * 2 + T * K * 8 + (3 if emb.dtype == torch.bfloat16 else 2) * ((E + 15) // 16 * 16) * d * 2
+    peak, _ = measured_peaks()
+    gbs = nbytes / (us / 1e6) / 1e9
+    return {"kernel": "route_kernel (gate GEMM + softmax + top-K)", "us": us, "tokens_per_s": T / (us / 1e6),
+            "algorithmic_bytes": nbytes, "achieved_gbs": gbs, "peak_gbs": peak, "frac": gbs / peak,
+            "traffic": committed_traffic("route_kernel", c["name"]),
+            "note": "median device time per launch, L2 flushed before each; bytes = tokens read once + "
+                    "outputs + the prepared gate weights once"}
+
+
 def gpu_arm(args):
     import torch
     import torch.distributed as dist
@@ -475,6 +514,13 @@ def gpu_arm(args):
         dist.all_reduce(stage, op=dist.ReduceOp.MAX)
     mean_pack, mean_mid, mean_expert, mean_unperm = stage.tolist()
 
+    # The router (gate GEMM + softmax + top-K) on the same tokens, timed alone
+    # with the same L2 flush: the step before the packing path in the
+    # reference's bench_e2e pipeline (apps/bench_e2e.cu:231-246).
+    router = None
+    if world == 1 and not layer and not args.no_router:
+        router = router_leg(mb, c, emb, stream, dev, flusher, args.steps, warm)
+
     # e2e through the C ABI with pinned host buffers (N = 1, identity expert)
     e2e = None
     if world == 1 and not args.no_e2e and not layer:
@@ -555,6 +601,8 @@ def gpu_arm(args):
                           if fused else "NCCL all_gather (counts) + 2 x all_to_all_single (rows)"}
         if e2e is not None:
             line["e2e"] = e2e
+        if router is not None:
+            line["router"] = router
         if world == 1 and not args.no_cpu_baseline and not layer:
             cv, per, kind = run_cpu(c, 1, c["T"], 5, 1, min_seconds=10.0)
             line["cpu_baseline"] = {
