@@ -25,6 +25,15 @@
 //      or ep_return_identity_kernel; then ep_signal_kernel raises back flags
 //   6. ep_wait_kernel (sender) waits for all back flags; unpermute reads the
 //      local back buffer
+// Replicated ("hot") experts: every rank holds its own copy of the experts in
+// a set H (the same on all ranks, moe_b200_ep_set_replicated); a row routed
+// to an expert of H never leaves its rank: the dispatch stores it into a local
+// block after the senders' blocks of the own receive buffer, and the expert
+// returns it to the own back buffer.  Receive buffer of rank r:
+//   [sender 0: r's non-replicated experts] ... [sender N-1: same] [own rows
+//   of the replicated experts, expert-major]
+// and r's local expert weights are ordered [non-replicated experts of its
+// range, ascending] + [replicated experts, ascending].
 // The host never waits inside a step.  This replaces the reference's
 // AllGather -> D2H -> host offsets -> grouped ncclSend/ncclRecv exchange
 // (apps/bench_prefill.cu:768-807, 889-906).  Every wait is bounded (the
@@ -49,13 +58,18 @@ cudaError_t launch_unpermute(const void* y, const float* packed_w, const int32_t
 int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* seg_expert, int nseg, int rows,
                         int d, int I, int E, const void* w_gate_up, const void* w_down, int dtype, void* h,
                         void* y, cudaStream_t s, char* const* dst_base, const int32_t* seg_src,
-                        const int32_t* seg_dst_row, int seg_groups);
+                        const int32_t* seg_dst_row, int seg_groups, int seg_group_len);
 
 constexpr int kEpMaxRanks = 64;
+
+constexpr int kEpMaxExperts = 1024;
 
 struct EpGeom {
     int nranks, rank, E, K, d, max_tokens;
     int first[kEpMaxRanks + 1];
+    uint32_t hot[kEpMaxExperts / 32];  // replicated experts (bit e)
+    int nhot;                          // |H|
+    int lrange;                        // experts of this rank's range that are not replicated
     size_t off_cflag, off_dflag, off_bflag, off_inbox, off_recv, off_back, total;
     int64_t recv_cap;
     uint64_t timeout_ns;
@@ -75,6 +89,10 @@ struct EpContext {
 static size_t al4k(size_t x) { return (x + 4095) & ~size_t(4095); }
 
 // ---------------------------------------------------------------- device ----
+
+__host__ __device__ __forceinline__ bool ep_is_hot(const EpGeom& g, int e) {
+    return (g.hot[e >> 5] >> (e & 31)) & 1u;
+}
 
 __device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
     uint64_t v;
@@ -127,9 +145,11 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
                         int32_t* __restrict__ slot_pos, WsHeader* __restrict__ hdr,
                         uint64_t* __restrict__ status, size_t status_words, uint64_t epoch,
                         uint32_t* __restrict__ dev_status) {
-    __shared__ int64_t dst_off[kEpMaxRanks];  // receive row of packed position p on rank r = dst_off[r] + p
     __shared__ int s_fail;
-    extern __shared__ int32_t s_owner[];      // [E]
+    // per expert e: the rank whose receive buffer takes its rows, and the
+    // receive row of packed position p there = s_dst[e] + p
+    extern __shared__ int64_t s_dst[];                          // [E]
+    int32_t* s_owner = reinterpret_cast<int32_t*>(s_dst + g.E);  // [E]
     const int K = g.K, nvec = g.d / 8;
     if (threadIdx.x == 0) s_fail = 0;
     __syncthreads();
@@ -139,17 +159,33 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
     wait_flags(reinterpret_cast<const uint64_t*>(mine + g.off_cflag), g.nranks, epoch, g.timeout_ns, dev_status,
                &s_fail);
     const int32_t* inbox = reinterpret_cast<const int32_t*>(mine + g.off_inbox);
-    for (int e = threadIdx.x; e < g.E; e += blockDim.x) {
-        int r = 0;
-        while (r + 1 < g.nranks && g.first[r + 1] <= e) ++r;
-        s_owner[e] = r;
-    }
+    const int32_t* own = inbox + size_t(g.rank) * g.E;  // this rank's counts
     if (threadIdx.x < g.nranks) {
+        // receiver r: this sender's block follows the blocks of senders < rank;
+        // inside it, r's non-replicated experts in ascending order
         const int r = threadIdx.x;
         int64_t base = 0;
         for (int s = 0; s < g.rank; ++s)
-            for (int e = g.first[r]; e < g.first[r + 1]; ++e) base += inbox[s * g.E + e];
-        dst_off[r] = base - expert_start[g.first[r]];
+            for (int e = g.first[r]; e < g.first[r + 1]; ++e)
+                if (!ep_is_hot(g, e)) base += inbox[s * g.E + e];
+        for (int e = g.first[r]; e < g.first[r + 1]; ++e) {
+            if (ep_is_hot(g, e)) continue;
+            s_owner[e] = r;
+            s_dst[e] = base - expert_start[e];
+            base += own[e];
+        }
+    } else if (threadIdx.x == g.nranks && g.nhot > 0) {
+        // replicated experts: the local block after every sender's block
+        int64_t base = 0;
+        for (int s = 0; s < g.nranks; ++s)
+            for (int e = g.first[g.rank]; e < g.first[g.rank + 1]; ++e)
+                if (!ep_is_hot(g, e)) base += inbox[s * g.E + e];
+        for (int e = 0; e < g.E; ++e) {
+            if (!ep_is_hot(g, e)) continue;
+            s_owner[e] = g.rank;
+            s_dst[e] = base - expert_start[e];
+            base += own[e];
+        }
     }
     __syncthreads();
 
@@ -170,7 +206,7 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
                 perm[p] = int32_t(t);
                 if (packed_w) packed_w[p] = __ldg(wts + sidx);
                 const int owner = s_owner[e];
-                dst_lane = reinterpret_cast<uint4*>(peer[owner] + g.off_recv + size_t(dst_off[owner] + p) * rowb);
+                dst_lane = reinterpret_cast<uint4*>(peer[owner] + g.off_recv + size_t(s_dst[e] + p) * rowb);
             }
             if (slot_pos) slot_pos[sidx] = p;
         }
@@ -225,19 +261,33 @@ ep_receive_kernel(EpGeom g, char* const* __restrict__ peer, uint64_t epoch, int3
     wait_flags(reinterpret_cast<const uint64_t*>(mine + g.off_dflag), g.nranks, epoch, g.timeout_ns, dev_status,
                &s_fail);
     const int32_t* inbox = reinterpret_cast<const int32_t*>(mine + g.off_inbox);
-    const int lo = g.first[g.rank], L = g.first[g.rank + 1] - lo;
-    const int nseg = g.nranks * L;
+    // local experts: [non-replicated experts of the range] + [replicated]
+    __shared__ int16_t s_local[kEpMaxExperts];
+    if (threadIdx.x == 0) {
+        int n = 0;
+        for (int e = g.first[g.rank]; e < g.first[g.rank + 1]; ++e)
+            if (!ep_is_hot(g, e)) s_local[n++] = int16_t(e);
+        for (int e = 0; e < g.E; ++e)
+            if (ep_is_hot(g, e)) s_local[n++] = int16_t(e);
+    }
+    __syncthreads();
+    const int L = g.lrange;
+    const int nseg = g.nranks * L + g.nhot;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     for (int base = 0; base < nseg; base += blockDim.x) {
         const int i = base + tid;
         int32_t v = 0;
         if (i < nseg) {
-            const int s = i / L, j = i % L;
-            v = inbox[s * g.E + lo + j];
+            // sender-major blocks of the range experts, then the own rows of
+            // the replicated experts
+            const bool tail = i >= g.nranks * L;
+            const int s = tail ? g.rank : i / L, j = tail ? L + (i - g.nranks * L) : i % L;
+            const int e_glob = s_local[j];
+            v = inbox[s * g.E + e_glob];
             seg_expert[i] = j;
             seg_src[i] = s;
-            int32_t before = 0;  // sender s's packed start of expert lo + j
-            for (int e = 0; e < lo + j; ++e) before += inbox[s * g.E + e];
+            int32_t before = 0;  // sender s's packed start of expert e_glob
+            for (int e = 0; e < e_glob; ++e) before += inbox[s * g.E + e];
             seg_dst_row[i] = before;
         }
         int32_t incl = v;
@@ -268,27 +318,30 @@ ep_return_identity_kernel(EpGeom g, char* const* __restrict__ back, const uint4*
                           const int32_t* __restrict__ seg_start, const int32_t* __restrict__ seg_src,
                           const int32_t* __restrict__ seg_dst_row, int nseg) {
     pdl_wait_primary();
-    __shared__ int64_t s_lo[kEpMaxRanks + 1];
+    __shared__ int64_t s_lo[kEpMaxRanks + 2];
     __shared__ int64_t s_max;
-    const int N = g.nranks, L = nseg / N;
+    // blocks q < N: the rows sender q sent (segments [q*L, (q+1)*L));
+    // block N: this rank's own rows of the replicated experts
+    const int N = g.nranks, L = g.lrange, NB = N + 1;
     if (threadIdx.x <= N) s_lo[threadIdx.x] = seg_start[threadIdx.x * L];
+    if (threadIdx.x == 0) s_lo[NB] = seg_start[nseg];
     __syncthreads();
     if (threadIdx.x == 0) {
         int64_t m = 0;
-        for (int q = 0; q < N; ++q) m = max(m, s_lo[q + 1] - s_lo[q]);
+        for (int q = 0; q < NB; ++q) m = max(m, s_lo[q + 1] - s_lo[q]);
         s_max = m;
     }
     __syncthreads();
     const int nvec = g.d / 8;
     const int lane = threadIdx.x & 31;
-    const int64_t total = s_max * N;
+    const int64_t total = s_max * NB;
     const int64_t gw = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int64_t nw = int64_t(gridDim.x) * (blockDim.x >> 5);
     for (int64_t q = gw; q < total; q += nw) {
-        const int snd = int(q % N);
-        const int64_t row = s_lo[snd] + q / N;
+        const int snd = int(q % NB);
+        const int64_t row = s_lo[snd] + q / NB;
         if (row >= s_lo[snd + 1]) continue;
-        int lo = snd * L, hi = lo + L - 1;   // segment of this row within the sender's range
+        int lo = snd * L, hi = (snd < N ? lo + L : nseg) - 1;   // segment of this row within its block
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
             if (seg_start[mid] <= row) lo = mid;
@@ -349,6 +402,7 @@ int moe_b200_ep_create(int nranks, int rank, int E, int K, int d, int max_tokens
                     "ep_create: need 1<=nranks<=%d, 0<=rank<nranks, E>=nranks, 1<=K<=32, d%%8==0, "
                     "max_tokens>=1, timeout_ms>=1",
                     kEpMaxRanks);
+    if (E > kEpMaxExperts) return fail(MOE_B200_ERR_UNSUPPORTED, "ep_create: E=%d above %d", E, kEpMaxExperts);
     if (expert_first[0] != 0 || expert_first[nranks] != E)
         return fail(MOE_B200_ERR_INVALID_ARG, "ep_create: expert_first must run from 0 to E");
     EpContext* ctx = new EpContext();
@@ -366,6 +420,9 @@ int moe_b200_ep_create(int nranks, int rank, int E, int K, int d, int max_tokens
             return fail(MOE_B200_ERR_INVALID_ARG, "ep_create: every rank must own at least one expert");
         }
     }
+    std::memset(g.hot, 0, sizeof(g.hot));
+    g.nhot = 0;
+    g.lrange = g.first[rank + 1] - g.first[rank];
     g.off_cflag = 0;
     g.off_dflag = 8 * kEpMaxRanks;
     g.off_bflag = 16 * kEpMaxRanks;
@@ -387,6 +444,46 @@ int moe_b200_ep_create(int nranks, int rank, int E, int K, int d, int max_tokens
     ctx->back_dev = ctx->peer_dev + kEpMaxRanks;
     *ctx_out = ctx;
     return MOE_B200_OK;
+}
+
+int moe_b200_ep_set_replicated(void* c, const int32_t* experts, int n) {
+    EpContext* ctx = as_ctx(c);
+    if (!ctx || (n > 0 && !experts)) return fail(MOE_B200_ERR_INVALID_ARG, "ep_set_replicated: null pointer");
+    EpGeom& g = ctx->g;
+    if (n < 0 || n > g.E) return fail(MOE_B200_ERR_INVALID_ARG, "ep_set_replicated: n=%d outside [0, E]", n);
+    uint32_t hot[kEpMaxExperts / 32] = {};
+    for (int i = 0; i < n; ++i) {
+        const int e = experts[i];
+        if (e < 0 || e >= g.E) return fail(MOE_B200_ERR_INVALID_ARG, "ep_set_replicated: expert %d outside [0, E)", e);
+        if ((hot[e >> 5] >> (e & 31)) & 1u)
+            return fail(MOE_B200_ERR_INVALID_ARG, "ep_set_replicated: expert %d listed twice", e);
+        hot[e >> 5] |= 1u << (e & 31);
+    }
+    std::memcpy(g.hot, hot, sizeof(hot));
+    g.nhot = n;
+    int lr = 0;
+    for (int e = g.first[g.rank]; e < g.first[g.rank + 1]; ++e)
+        if (!ep_is_hot(g, e)) ++lr;
+    g.lrange = lr;
+    return MOE_B200_OK;
+}
+
+int moe_b200_ep_local_experts(void* c, int32_t* experts_out) {
+    EpContext* ctx = as_ctx(c);
+    if (!ctx) return -1;
+    const EpGeom& g = ctx->g;
+    int n = 0;
+    for (int e = g.first[g.rank]; e < g.first[g.rank + 1]; ++e)
+        if (!ep_is_hot(g, e)) {
+            if (experts_out) experts_out[n] = e;
+            ++n;
+        }
+    for (int e = 0; e < g.E; ++e)
+        if (ep_is_hot(g, e)) {
+            if (experts_out) experts_out[n] = e;
+            ++n;
+        }
+    return n;
 }
 
 int moe_b200_ep_destroy(void* c) {
@@ -481,7 +578,7 @@ int moe_b200_ep_dispatch(void* c, uint64_t epoch, const void* emb, const int32_t
         int grid = sm_count_ep() * 4;
         const int want = (T + 7) / 8;
         if (grid > want) grid = want;
-        cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(256), size_t(g.E) * 4, s);
+        cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(256), size_t(g.E) * 12, s);
         cudaLaunchAttribute attr = pdl_attr();
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
@@ -515,7 +612,7 @@ int moe_b200_ep_return_identity(void* c, uint64_t epoch, const int32_t* seg_star
     EpContext* ctx = as_ctx(c);
     if (!ctx || !ctx->connected) return fail(MOE_B200_ERR_INVALID_ARG, "ep_return_identity: not connected");
     const EpGeom& g = ctx->g;
-    const int nseg = g.nranks * (g.first[g.rank + 1] - g.first[g.rank]);
+    const int nseg = g.nranks * g.lrange + g.nhot;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaLaunchConfig_t cfg = pdl_config(dim3(sm_count_ep() * 4), dim3(256), 0, s);
     cudaLaunchAttribute attr = pdl_attr();
@@ -537,13 +634,14 @@ int moe_b200_ep_ffn_return(void* c, uint64_t epoch, const int32_t* seg_start, co
     EpContext* ctx = as_ctx(c);
     if (!ctx || !ctx->connected) return fail(MOE_B200_ERR_INVALID_ARG, "ep_ffn_return: not connected");
     const EpGeom& g = ctx->g;
-    const int L = g.first[g.rank + 1] - g.first[g.rank];
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // GEMM 2's epilogue stores each finished tile straight into the back
-    // buffer of the rank that sent its rows (scatter mode).
-    int st = grouped_swiglu_impl(ctx->region + g.off_recv, seg_start, seg_expert, g.nranks * L, int(g.recv_cap), g.d,
-                                 I, L, w_gate_up, w_down, dtype, h, ctx->region + g.off_recv, s, ctx->back_dev,
-                                 seg_src, seg_dst_row, g.nranks);
+    // buffer of the rank that sent its rows (scatter mode).  Local experts:
+    // the range's non-replicated ones, then the replicated ones.
+    int st = grouped_swiglu_impl(ctx->region + g.off_recv, seg_start, seg_expert, g.nranks * g.lrange + g.nhot,
+                                 int(g.recv_cap), g.d, I, g.lrange + g.nhot, w_gate_up, w_down, dtype, h,
+                                 ctx->region + g.off_recv, s, ctx->back_dev, seg_src, seg_dst_row, g.nranks,
+                                 g.lrange);
     if (st != MOE_B200_OK) return st;
     ep_signal_kernel<<<1, 64, 0, s>>>(g, ctx->peer_dev, g.off_bflag, epoch);
     cudaError_t err = cudaGetLastError();

@@ -204,7 +204,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                     int gate_up_split, uint16_t* __restrict__ out, int64_t out_stride,
                     uint32_t* __restrict__ dev_status, char* const* __restrict__ dst_base,
                     const int32_t* __restrict__ seg_src, const int32_t* __restrict__ seg_dst_row,
-                    int seg_groups) {
+                    int seg_groups, int seg_group_len) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte aligned stage buffers (SW128 atoms), control block after them.
     unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -229,7 +229,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     volatile int* abort_flag = &ctl->abort_flag;
     const int G = seg_groups > 1 ? seg_groups : 1;
-    const int Lg = nseg / G;
+    const int Lg = G > 1 ? seg_group_len : 0;
+    const int GL = G * Lg;  // segments in the interleaved groups; later ones keep their order
     // CTA-pair coordinates (CG = 2): rank 0 is the leader that issues the MMAs.
     const uint32_t crank = CG == 2 ? cluster_rank() : 0u;
     const int tile0 = CG == 2 ? int(cluster_id_x()) : int(blockIdx.x);
@@ -250,11 +251,12 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     }
     if (warp == 0) {
         // Tiles walk the segments in "tile order": with seg_groups = G > 1 the
-        // nseg = G * L segments (stored group-major: group q, item j at q*L+j)
-        // are visited item-major (j*G + q), so consecutive row blocks share an
-        // expert and rotate over the groups (the senders, whose buffers the
-        // scatter epilogue writes to).  blk_prefix[i] = row blocks of the
-        // segments before tile-order position i.
+        // first G * L segments (L = seg_group_len; stored group-major: group
+        // q, item j at q*L+j) are visited item-major (j*G + q), so consecutive
+        // row blocks share an expert and rotate over the groups (the senders,
+        // whose buffers the scatter epilogue writes to); segments after them
+        // keep their order.  blk_prefix[i] = row blocks of the segments
+        // before tile-order position i.
         int run = 0;
         for (int s0 = 0; s0 < nseg; s0 += 32) {
             int i = s0 + lane;
@@ -264,7 +266,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                 s_start[i] = lo;
                 s_expsrc[i] = (seg_expert ? seg_expert[i] : i) | (dst_base ? seg_src[i] << 16 : 0);
                 if (dst_base) s_dst_row[i] = seg_dst_row[i];
-                const int nat = G > 1 ? (i % G) * Lg + i / G : i;  // segment at tile-order position i
+                const int nat = i < GL ? (i % G) * Lg + i / G : i;  // segment at tile-order position i
                 const int rows = seg_start[nat + 1] - seg_start[nat];
                 cnt = rows > 0 ? (rows + kBlockRows - 1) / kBlockRows : 0;
             }
@@ -319,7 +321,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             for (int tile = tile0; tile < total_tiles && !*abort_flag; tile += tile_step) {
                 const int g = tile / n_blocks, n = tile % n_blocks;
                 const int ti = find_segment(blk_prefix, nseg, g);
-                const int s = G > 1 ? (ti % G) * Lg + ti / G : ti;
+                const int s = ti < GL ? (ti % G) * Lg + ti / G : ti;
                 const int e = s_expsrc[s] & 0xffff;
                 const int row0 = s_start[s] + (g - blk_prefix[ti]) * kBlockRows + int(crank) * kTileM;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
@@ -410,7 +412,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             tc_fence_after();
             const int g = tile / n_blocks, n = tile % n_blocks;
             const int ti = find_segment(blk_prefix, nseg, g);
-            const int s = G > 1 ? (ti % G) * Lg + ti / G : ti;
+            const int s = ti < GL ? (ti % G) * Lg + ti / G : ti;
             const int blk = g - blk_prefix[ti];
             const int seg_rows = s_start[s + 1] - s_start[s];
             // This warp's 32 rows start at segment row w_row0; nrows_w of them are in the segment.
@@ -528,7 +530,7 @@ static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb_, co
                                int n_out, int n_blocks, int split, void* out, int64_t out_stride,
                                uint32_t* st, cudaStream_t stream, char* const* dst_base = nullptr,
                                const int32_t* seg_src = nullptr, const int32_t* seg_dst_row = nullptr,
-                               int seg_groups = 1) {
+                               int seg_groups = 1, int seg_group_len = 0) {
     const size_t smem = ffn_smem_bytes<CG>(nseg);
     auto kern = grouped_gemm_kernel<EPI, DT, CG>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -555,7 +557,7 @@ static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb_, co
     cfg.gridDim = dim3(CG * groups);
     return cudaLaunchKernelEx(&cfg, kern, ma, mb_, seg_start, seg_expert, nseg, kdim, b_rows_per_expert, n_out,
                               n_blocks, split, static_cast<uint16_t*>(out), out_stride, st, dst_base, seg_src,
-                              seg_dst_row, seg_groups);
+                              seg_dst_row, seg_groups, seg_group_len);
 }
 
 template <int DT>
@@ -563,19 +565,19 @@ static cudaError_t launch_ffn(int cg, const CUtensorMap& mx, const CUtensorMap& 
                               const CUtensorMap& mwd, const int32_t* seg_start, const int32_t* seg_expert, int nseg,
                               int rows, int d, int I, void* h, void* y, uint32_t* st, cudaStream_t s,
                               char* const* dst_base, const int32_t* seg_src, const int32_t* seg_dst_row,
-                              int seg_groups) {
+                              int seg_groups, int seg_group_len) {
     const int nb1 = (I + kTileN / 2 - 1) / (kTileN / 2);
     const int nb2 = (d + kTileN - 1) / kTileN;
     cudaError_t err =
         (cg & 1) ? launch_gemm<kEpiSwiGLU, DT, 2>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1, I, h,
-                                                  I, st, s, nullptr, nullptr, nullptr, seg_groups)
+                                                  I, st, s, nullptr, nullptr, nullptr, seg_groups, seg_group_len)
                  : launch_gemm<kEpiSwiGLU, DT, 1>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1, I, h,
-                                                  I, st, s, nullptr, nullptr, nullptr, seg_groups);
+                                                  I, st, s, nullptr, nullptr, nullptr, seg_groups, seg_group_len);
     if (err != cudaSuccess) return err;
     return (cg & 2) ? launch_gemm<kEpiStore, DT, 2>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0, y, d,
-                                                    st, s, dst_base, seg_src, seg_dst_row, seg_groups)
+                                                    st, s, dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len)
                     : launch_gemm<kEpiStore, DT, 1>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0, y, d,
-                                                    st, s, dst_base, seg_src, seg_dst_row, seg_groups);
+                                                    st, s, dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len);
 }
 
 int fail(int code, const char* fmt, ...);
@@ -587,7 +589,7 @@ namespace moe_b200 {
 int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* seg_expert, int nseg, int rows,
                         int d, int I, int E, const void* w_gate_up, const void* w_down, int dtype, void* h,
                         void* y, cudaStream_t s, char* const* dst_base, const int32_t* seg_src,
-                        const int32_t* seg_dst_row, int seg_groups) {
+                        const int32_t* seg_dst_row, int seg_groups, int seg_group_len) {
     if (nseg < 1 || rows < 0 || d < 1 || I < 1 || E < 1)
         return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: need nseg>=1, rows>=0, d>=1, I>=1, E>=1");
     if (nseg > kMaxSegments)
@@ -619,9 +621,9 @@ int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* 
     const cudaError_t err =
         dtype == MOE_B200_BF16
             ? launch_ffn<MOE_B200_BF16>(cg, mx, mwgu, mh, mwd, seg_start, seg_expert, nseg, rows, d, I, h, y, st, s,
-                                        dst_base, seg_src, seg_dst_row, seg_groups)
+                                        dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len)
             : launch_ffn<MOE_B200_F16>(cg, mx, mwgu, mh, mwd, seg_start, seg_expert, nseg, rows, d, I, h, y, st, s,
-                                       dst_base, seg_src, seg_dst_row, seg_groups);
+                                       dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len);
     return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "grouped_swiglu launch");
 }
 }  // namespace moe_b200
@@ -630,5 +632,5 @@ extern "C" int moe_b200_grouped_swiglu(const void* x, const int32_t* seg_start, 
                                        int nseg, int rows, int d, int I, int E, const void* w_gate_up,
                                        const void* w_down, int dtype, void* h, void* y, void* stream) {
     return moe_b200::grouped_swiglu_impl(x, seg_start, seg_expert, nseg, rows, d, I, E, w_gate_up, w_down, dtype,
-                                         h, y, static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr, 1);
+                                         h, y, static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr, 1, 0);
 }

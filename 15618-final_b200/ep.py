@@ -171,10 +171,16 @@ class FusedExpertParallel:
     (moe_b200_ep_*) for the protocol; replaces the reference's host-synchronised
     NCCL exchange (apps/bench_prefill.cu:768-807, 889-906).
 
-    Every rank must run the same sequence of steps (epochs advance together)."""
+    Every rank must run the same sequence of steps (epochs advance together).
+
+    `replicated`: global expert ids every rank holds a copy of (the same list
+    on every rank); their rows never leave their rank.  `local_experts` lists
+    the global ids of this rank's expert weights in the order ffn_return
+    expects: the non-replicated experts of its range, then the replicated
+    ones."""
 
     def __init__(self, E: int, K: int, d: int, max_tokens: int, dtype, group=None, device=None,
-                 timeout_ms: int = 2000):
+                 timeout_ms: int = 2000, replicated=()):
         import ctypes
         import torch
         import torch.distributed as dist
@@ -195,6 +201,15 @@ class FusedExpertParallel:
         self.ctx = ctypes.c_void_p()
         mb._check(self.L_.moe_b200_ep_create(self.N, self.rank, E, K, d, max_tokens, first, timeout_ms,
                                              ctypes.byref(self.ctx)), "ep_create")
+        rep_ids = sorted(set(int(e) for e in replicated))
+        arr = (ctypes.c_int32 * max(1, len(rep_ids)))(*rep_ids)
+        mb._check(self.L_.moe_b200_ep_set_replicated(self.ctx, arr, len(rep_ids)), "ep_set_replicated")
+        self.replicated = rep_ids
+        n_local = self.L_.moe_b200_ep_local_experts(self.ctx, None)
+        loc = (ctypes.c_int32 * n_local)()
+        self.L_.moe_b200_ep_local_experts(self.ctx, loc)
+        self.local_experts = list(loc)
+        self.L_range = n_local - len(rep_ids)   # non-replicated experts of this rank's range
         h = (ctypes.c_uint8 * 64)()
         mb._check(self.L_.moe_b200_ep_ipc_handle(self.ctx, h), "ep_ipc_handle")
         mine = torch.tensor(list(h), dtype=torch.uint8, device=device)
@@ -206,7 +221,7 @@ class FusedExpertParallel:
         buf = (ctypes.c_uint8 * (self.N * 64))(*allh.cpu().tolist())
         mb._check(self.L_.moe_b200_ep_connect(self.ctx, buf), "ep_connect")
         self.epoch = 0
-        nseg = self.N * self.L
+        nseg = self.N * self.L_range + len(rep_ids)
         mk = lambda n: torch.empty(n, dtype=torch.int32, device=device)
         self.seg_start, self.seg_expert, self.seg_src, self.seg_dst_row = mk(nseg + 1), mk(nseg), mk(nseg), mk(nseg)
         self.recv_cap = int(self.L_.moe_b200_ep_recv_capacity(self.ctx))
@@ -243,8 +258,9 @@ class FusedExpertParallel:
                        "ep_return_identity")
 
     def ffn_return(self, w_gate_up, w_down, h, stream=None):
-        """Grouped SwiGLU on the received rows (local experts' weights
-        [L, 2I, d] / [L, d, I]); h: [recv_capacity, I] scratch."""
+        """Grouped SwiGLU on the received rows: w_gate_up [n, 2I, d] /
+        w_down [n, d, I] for the n = len(local_experts) local experts in
+        local_experts order; h: [recv_capacity, I] scratch."""
         p = self.mb._ptr
         I = w_down.shape[2]
         self.mb._check(self.L_.moe_b200_ep_ffn_return(

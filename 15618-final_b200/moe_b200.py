@@ -89,6 +89,10 @@ def lib() -> ctypes.CDLL:
     L.moe_b200_ep_create.restype = cint
     L.moe_b200_ep_create.argtypes = [cint, cint, cint, cint, cint, cint, ctypes.POINTER(ctypes.c_int32), cint,
                                      ctypes.POINTER(vp)]
+    L.moe_b200_ep_set_replicated.restype = cint
+    L.moe_b200_ep_set_replicated.argtypes = [vp, ctypes.POINTER(ctypes.c_int32), cint]
+    L.moe_b200_ep_local_experts.restype = cint
+    L.moe_b200_ep_local_experts.argtypes = [vp, ctypes.POINTER(ctypes.c_int32)]
     L.moe_b200_ep_destroy.restype = cint
     L.moe_b200_ep_destroy.argtypes = [vp]
     L.moe_b200_ep_ipc_handle.restype = cint

@@ -54,6 +54,9 @@ def parse():
                          "reference's contiguous ranges")
     ap.add_argument("--no-router", action="store_true",
                     help="skip the separate router timing (N=1 pack configs)")
+    ap.add_argument("--replicate", type=int, default=8,
+                    help="N>1 fused EP: the R most popular experts get a copy on every rank, so their rows "
+                         "stay local (0 = the reference's pure partition)")
     ap.add_argument("--ep", default="fused", choices=["fused", "nccl"],
                     help="N>1 exchange: fused peer-store kernels (default) or NCCL AllToAllv")
     return ap.parse_args()
@@ -391,6 +394,16 @@ def gpu_arm(args):
     flusher = L2Flush(dev)
     bounds = ep.expert_ranges(E, world)
     lo, hi = bounds[rank], bounds[rank + 1]
+    fused = world > 1 and args.ep == "fused"
+    # the most popular experts (routing.gen_routing: popularity falls with the
+    # expert index), by their labels under the placement
+    replicated = sorted(label[e] for e in range(min(args.replicate, E))) if fused else []
+    if fused:
+        with torch.cuda.stream(stream):
+            fep = ep.FusedExpertParallel(E, K, d, T, tdtype, device=dev, timeout_ms=5000, replicated=replicated)
+        local_labels = fep.local_experts
+    else:
+        local_labels = list(range(lo, hi))
     with torch.cuda.stream(stream):
         ws = mb.Workspace(T, K, E, device=dev, stream=stream)
         bufs = mb.pack(emb, asgn, wts, E, workspace=ws, stream=stream)
@@ -399,9 +412,10 @@ def gpu_arm(args):
             I = c["I"]
             # random-init experts ~N(0, 0.02), seeded by GLOBAL expert id so every
             # rank count uses the same weights (apps/bench_prefill.cu:432-439)
-            wgu = torch.empty((hi - lo, 2 * I, d), dtype=tdtype, device=dev)
-            wdn = torch.empty((hi - lo, d, I), dtype=tdtype, device=dev)
-            for j, lab in enumerate(range(lo, hi)):
+            nl = len(local_labels)
+            wgu = torch.empty((nl, 2 * I, d), dtype=tdtype, device=dev)
+            wdn = torch.empty((nl, d, I), dtype=tdtype, device=dev)
+            for j, lab in enumerate(local_labels):
                 g = torch.Generator(device=dev)
                 g.manual_seed(1000 + orig_of[lab])
                 wgu[j] = (torch.randn((2 * I, d), generator=g, device=dev) * 0.02).to(tdtype)
@@ -409,16 +423,13 @@ def gpu_arm(args):
             cap = world * TK if world > 1 else TK
             h_buf = torch.empty((cap, I), dtype=tdtype, device=dev)
             y_buf = torch.empty((cap, d), dtype=tdtype, device=dev)
-    fused = world > 1 and args.ep == "fused"
     if world > 1 and not fused:
         epx = ep.ExpertParallel(E, device=dev)
         recv_buf = torch.empty((world * TK, d), dtype=tdtype, device=dev)
         back_buf = torch.empty((TK, d), dtype=tdtype, device=dev)
-    if fused:
+    if fused and layer:
         with torch.cuda.stream(stream):
-            fep = ep.FusedExpertParallel(E, K, d, T, tdtype, device=dev, timeout_ms=5000)
-            if layer:
-                h_buf = torch.empty((fep.recv_cap, c["I"]), dtype=tdtype, device=dev)
+            h_buf = torch.empty((fep.recv_cap, c["I"]), dtype=tdtype, device=dev)
 
     def step(split=False):
         """One pass.  Returns CUDA events recorded on the launching stream: the
@@ -593,6 +604,8 @@ def gpu_arm(args):
             }
         if world > 1:
             line["ep"] = {"experts_per_rank": [bounds[g + 1] - bounds[g] for g in range(world)],
+                          "replicated": (f"{len(replicated)} most popular experts have a copy on every rank "
+                                         "(their rows stay local)") if replicated else "none",
                           "placement": args.placement + (" (expert e -> rank e % N by popularity rank)"
                                                          if args.placement == "balanced" else ""),
                           "exchange": ("fused: pack stores rows into the owners' receive buffers over NVLink, "

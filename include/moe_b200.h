@@ -226,8 +226,9 @@ int moe_b200_ep_layout(const int32_t* all_counts, int nranks, int E, int rank,
  *                                 store every token row straight into the
  *                                 receive buffer of the rank owning its expert
  *   moe_b200_ep_receive           wait for all senders; segment table of the
- *                                 receive buffer (seg_* arrays of nranks*L(+1),
- *                                 L = this rank's experts)
+ *                                 receive buffer (seg_* arrays of
+ *                                 nranks*L' + H (+1) entries: L' = this rank's
+ *                                 non-replicated experts, H = replicated ones)
  *   moe_b200_ep_ffn_return        grouped SwiGLU on the received rows whose
  *                                 down-GEMM stores every row straight into
  *                                 the sender's back buffer
@@ -241,6 +242,17 @@ int moe_b200_ep_create(int nranks, int rank, int E, int K, int d, int max_tokens
                        const int32_t* expert_first /* host, nranks+1 */, int timeout_ms,
                        void** ctx /* host, out */);
 int moe_b200_ep_destroy(void* ctx);
+/* Replicated experts (no reference counterpart; the reference partitions the
+ * experts contiguously, apps/bench_prefill.cu:361): every rank holds its own
+ * copy of experts[0..n-1], and rows routed to them stay on their rank (no
+ * NVLink traffic); the other experts keep their owner ranks.  Call before
+ * the first step with the same set on every rank.  The rank's local expert
+ * weights (moe_b200_ep_ffn_return) are then ordered as
+ * moe_b200_ep_local_experts lists them: the non-replicated experts of its
+ * range, then the replicated ones, each ascending.  Returns the count;
+ * experts_out (host, may be NULL) receives the global ids.                 */
+int moe_b200_ep_set_replicated(void* ctx, const int32_t* experts /* host */, int n);
+int moe_b200_ep_local_experts(void* ctx, int32_t* experts_out /* host, may be NULL */);
 int moe_b200_ep_ipc_handle(void* ctx, void* handle /* host, 64 bytes out */);
 int moe_b200_ep_connect(void* ctx, const void* handles /* host, nranks*64 bytes */);
 void* moe_b200_ep_recv_rows(void* ctx);

@@ -69,8 +69,9 @@ def run_fused_steps(epx, x, a, w, E, wgu_local, wdn_local, I, identity, steps, d
     return res, ws
 
 
+@pytest.mark.parametrize("replicated", [(), (0, 3, 5)])
 @pytest.mark.parametrize("identity", [True, False])
-def test_fused_ep_single_rank_matches_single_gpu_layer(cuda, identity):
+def test_fused_ep_single_rank_matches_single_gpu_layer(cuda, identity, replicated):
     T, K, E, d, I = 2048, 4, 16, 256, 128
     dtype = torch.bfloat16
     asgn, wts = routing.gen_routing(T, K, E, "zipf", seed=3)
@@ -78,9 +79,13 @@ def test_fused_ep_single_rank_matches_single_gpu_layer(cuda, identity):
     a = torch.from_numpy(asgn).cuda()
     w = torch.from_numpy(wts).cuda()
     wgu, wdn = make_weights(E, d, I, dtype, "cuda")
-    epx = ep.FusedExpertParallel(E, K, d, T, dtype, device="cuda")
+    epx = ep.FusedExpertParallel(E, K, d, T, dtype, device="cuda", replicated=replicated)
     try:
-        outs, ws = run_fused_steps(epx, x, a, w, E, wgu, wdn, I, identity, 3, "cuda")
+        loc = epx.local_experts
+        assert sorted(loc) == list(range(E))
+        assert loc[len(loc) - len(replicated):] == sorted(replicated)
+        outs, ws = run_fused_steps(epx, x, a, w, E, wgu[loc].contiguous(), wdn[loc].contiguous(), I, identity, 3,
+                                   "cuda")
         assert mb.device_status() == 0
         assert ws.device_status() == 0
         want = single_gpu_layer(x, a, w, E, wgu, wdn, identity)
@@ -153,15 +158,18 @@ def _multi_worker(rank, world, port, results):
         asgn, wts = routing.gen_routing(T, K, E, "zipf", seed=50 + rank)
         x = routing.gen_rows(T, d, "bfloat16", seed=50 + rank, device=dev)
         a, w = torch.from_numpy(asgn).to(dev), torch.from_numpy(wts).to(dev)
-        for identity in (True, False):
-            epx = ep.FusedExpertParallel(E, K, d, T, dtype, device=dev, timeout_ms=5000)
-            lo, hi = epx.bounds[rank], epx.bounds[rank + 1]
-            outs, _ = run_fused_steps(epx, x, a, w, E, wgu[lo:hi].contiguous(), wdn[lo:hi].contiguous(), I,
-                                      identity, 3, dev)
-            want = single_gpu_layer(x, a, w, E, wgu, wdn, identity)
-            ok[identity] = all(torch.equal(y.view(torch.int16), want.view(torch.int16)) for y in outs)
-            ok[f"status{identity}"] = mb.device_status()
-            epx.close()
+        # without and with replicated experts (the hottest ones: rows stay local)
+        for replicated in ((), (0, 1, 7)):
+            for identity in (True, False):
+                epx = ep.FusedExpertParallel(E, K, d, T, dtype, device=dev, timeout_ms=5000, replicated=replicated)
+                loc = epx.local_experts
+                outs, _ = run_fused_steps(epx, x, a, w, E, wgu[loc].contiguous(), wdn[loc].contiguous(), I,
+                                          identity, 3, dev)
+                want = single_gpu_layer(x, a, w, E, wgu, wdn, identity)
+                key = (identity, len(replicated))
+                ok[key] = all(torch.equal(y.view(torch.int16), want.view(torch.int16)) for y in outs)
+                ok[("status",) + key] = mb.device_status()
+                epx.close()
         results[rank] = ok
     finally:
         dist.barrier()
@@ -181,5 +189,7 @@ def test_fused_ep_multi_gpu_matches_single_gpu():
         res = dict(results)
     assert not alive, "a rank did not finish"
     for r in range(world):
-        assert res[r][True] and res[r][False], res
-        assert res[r]["statusTrue"] == 0 and res[r]["statusFalse"] == 0, res
+        for nrep in (0, 3):
+            for identity in (True, False):
+                assert res[r][(identity, nrep)], res
+                assert res[r][("status", identity, nrep)] == 0, res
