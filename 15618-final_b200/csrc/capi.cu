@@ -89,8 +89,8 @@ int moe_b200_pack(const void* emb, const int32_t* asgn, const float* wts, int T,
         if (err == cudaSuccess) err = cudaMemsetAsync(expert_start, 0, size_t(E + 1) * 4, s);
         return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "pack (empty)");
     }
-    if (!emb || !asgn || !packed || !perm)
-        return fail(MOE_B200_ERR_INVALID_ARG, "pack: emb, asgn, packed and perm are required");
+    if (!asgn || !perm || (packed && !emb))
+        return fail(MOE_B200_ERR_INVALID_ARG, "pack: asgn and perm (and emb when packed is given) are required");
     if (packed_weights && !wts)
         return fail(MOE_B200_ERR_INVALID_ARG, "pack: packed_weights needs wts");
     const size_t need = plan_pack(T, K, E).total_bytes;

@@ -58,7 +58,8 @@ cudaError_t launch_unpermute(const void* y, const float* packed_w, const int32_t
 int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* seg_expert, int nseg, int rows,
                         int d, int I, int E, const void* w_gate_up, const void* w_down, int dtype, void* h,
                         void* y, cudaStream_t s, char* const* dst_base, const int32_t* seg_src,
-                        const int32_t* seg_dst_row, int seg_groups, int seg_group_len);
+                        const int32_t* seg_dst_row, int seg_groups, int seg_group_len, const int32_t* gather_rows,
+                        int gather_T);
 
 constexpr int kEpMaxRanks = 64;
 
@@ -641,7 +642,7 @@ int moe_b200_ep_ffn_return(void* c, uint64_t epoch, const int32_t* seg_start, co
     int st = grouped_swiglu_impl(ctx->region + g.off_recv, seg_start, seg_expert, g.nranks * g.lrange + g.nhot,
                                  int(g.recv_cap), g.d, I, g.lrange + g.nhot, w_gate_up, w_down, dtype, h,
                                  ctx->region + g.off_recv, s, ctx->back_dev, seg_src, seg_dst_row, g.nranks,
-                                 g.lrange);
+                                 g.lrange, nullptr, 0);
     if (st != MOE_B200_OK) return st;
     ep_signal_kernel<<<1, 64, 0, s>>>(g, ctx->peer_dev, g.off_bflag, epoch);
     cudaError_t err = cudaGetLastError();

@@ -204,7 +204,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                     int gate_up_split, uint16_t* __restrict__ out, int64_t out_stride,
                     uint32_t* __restrict__ dev_status, char* const* __restrict__ dst_base,
                     const int32_t* __restrict__ seg_src, const int32_t* __restrict__ seg_dst_row,
-                    int seg_groups, int seg_group_len) {
+                    int seg_groups, int seg_group_len, const int32_t* __restrict__ gather_rows,
+                    int gather_limit) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte aligned stage buffers (SW128 atoms), control block after them.
     unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -314,7 +315,51 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     const int nk = (kdim + kTileK - 1) / kTileK;
     const uint32_t leader_full0 = CG == 2 ? map_to_rank(&ctl->full[0], 0) : 0u;
 
-    if (warp == 0) {
+    if (warp == 0 && CG == 1 && gather_rows) {
+        // ---------------- TMA producer, gathered A rows ----------------
+        // Row i of a tile is token gather_rows[packed row]: each lane fetches
+        // 4 of the 128 rows per K step with one tile::gather4 load (a 1-row
+        // box of 64 columns; the 4 rows land as 512 contiguous bytes of the
+        // 128-byte-swizzled tile), lane 0 arms the barrier and loads B.
+        uint32_t it = 0;
+        const int total_rows = s_start[nseg];
+        for (int tile = tile0; tile < total_tiles && !*abort_flag; tile += tile_step) {
+            const int g = tile / n_blocks, n = tile % n_blocks;
+            const int ti = find_segment(blk_prefix, nseg, g);
+            const int s = ti < GL ? (ti % G) * Lg + ti / G : ti;
+            const int e = s_expsrc[s] & 0xffff;
+            const int row0 = s_start[s] + (g - blk_prefix[ti]) * kBlockRows;
+            int r4[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int p = row0 + lane * 4 + q;  // rows past the segment are masked in the epilogue
+                const int t = p < total_rows ? __ldg(gather_rows + p) : 0;
+                r4[q] = (t >= 0 && t < gather_limit) ? t : 0;
+            }
+            bool ok = true;
+            for (int kb = 0; kb < nk; ++kb, ++it) {
+                const int st = int(it % kStages);
+                if (lane == 0)
+                    ok = wait_or_abort(&ctl->empty[st], ((it / kStages) & 1u) ^ 1u, abort_flag, dev_status);
+                if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+                if (lane == 0) mbar_arrive_expect_tx(&ctl->full[st], kABytes + kBBytes);
+                __syncwarp();
+                tma_gather4(sA + st * kABytes + lane * 512, &tmap_a, kb * kTileK, r4[0], r4[1], r4[2], r4[3],
+                            &ctl->full[st]);
+                if (lane == 0) {
+                    unsigned char* b = sB + st * kBBytes;
+                    if (EPI == kEpiSwiGLU) {
+                        const int brow = e * b_rows_per_expert + n * (kTileN / 2);
+                        tma_load_2d(b, &tmap_b, kb * kTileK, brow, &ctl->full[st]);
+                        tma_load_2d(b + kBBytes / 2, &tmap_b, kb * kTileK, brow + gate_up_split, &ctl->full[st]);
+                    } else {
+                        tma_load_2d(b, &tmap_b, kb * kTileK, e * b_rows_per_expert + n * kTileN, &ctl->full[st]);
+                    }
+                }
+            }
+            if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+        }
+    } else if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             uint32_t it = 0;
@@ -530,7 +575,8 @@ static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb_, co
                                int n_out, int n_blocks, int split, void* out, int64_t out_stride,
                                uint32_t* st, cudaStream_t stream, char* const* dst_base = nullptr,
                                const int32_t* seg_src = nullptr, const int32_t* seg_dst_row = nullptr,
-                               int seg_groups = 1, int seg_group_len = 0) {
+                               int seg_groups = 1, int seg_group_len = 0, const int32_t* gather_rows = nullptr,
+                               int gather_limit = 0) {
     const size_t smem = ffn_smem_bytes<CG>(nseg);
     auto kern = grouped_gemm_kernel<EPI, DT, CG>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -557,7 +603,7 @@ static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb_, co
     cfg.gridDim = dim3(CG * groups);
     return cudaLaunchKernelEx(&cfg, kern, ma, mb_, seg_start, seg_expert, nseg, kdim, b_rows_per_expert, n_out,
                               n_blocks, split, static_cast<uint16_t*>(out), out_stride, st, dst_base, seg_src,
-                              seg_dst_row, seg_groups, seg_group_len);
+                              seg_dst_row, seg_groups, seg_group_len, gather_rows, gather_limit);
 }
 
 template <int DT>
@@ -565,14 +611,17 @@ static cudaError_t launch_ffn(int cg, const CUtensorMap& mx, const CUtensorMap& 
                               const CUtensorMap& mwd, const int32_t* seg_start, const int32_t* seg_expert, int nseg,
                               int rows, int d, int I, void* h, void* y, uint32_t* st, cudaStream_t s,
                               char* const* dst_base, const int32_t* seg_src, const int32_t* seg_dst_row,
-                              int seg_groups, int seg_group_len) {
+                              int seg_groups, int seg_group_len, const int32_t* gather_rows, int gather_T) {
     const int nb1 = (I + kTileN / 2 - 1) / (kTileN / 2);
     const int nb2 = (d + kTileN - 1) / kTileN;
+    // The gathered form of GEMM 1 runs on single SMs.
     cudaError_t err =
-        (cg & 1) ? launch_gemm<kEpiSwiGLU, DT, 2>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1, I, h,
-                                                  I, st, s, nullptr, nullptr, nullptr, seg_groups, seg_group_len)
-                 : launch_gemm<kEpiSwiGLU, DT, 1>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1, I, h,
-                                                  I, st, s, nullptr, nullptr, nullptr, seg_groups, seg_group_len);
+        ((cg & 1) && !gather_rows)
+            ? launch_gemm<kEpiSwiGLU, DT, 2>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1, I, h, I,
+                                             st, s, nullptr, nullptr, nullptr, seg_groups, seg_group_len)
+            : launch_gemm<kEpiSwiGLU, DT, 1>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1, I, h, I,
+                                             st, s, nullptr, nullptr, nullptr, seg_groups, seg_group_len, gather_rows,
+                                             gather_T);
     if (err != cudaSuccess) return err;
     return (cg & 2) ? launch_gemm<kEpiStore, DT, 2>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0, y, d,
                                                     st, s, dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len)
@@ -589,7 +638,8 @@ namespace moe_b200 {
 int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* seg_expert, int nseg, int rows,
                         int d, int I, int E, const void* w_gate_up, const void* w_down, int dtype, void* h,
                         void* y, cudaStream_t s, char* const* dst_base, const int32_t* seg_src,
-                        const int32_t* seg_dst_row, int seg_groups, int seg_group_len) {
+                        const int32_t* seg_dst_row, int seg_groups, int seg_group_len, const int32_t* gather_rows,
+                        int gather_T) {
     if (nseg < 1 || rows < 0 || d < 1 || I < 1 || E < 1)
         return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: need nseg>=1, rows>=0, d>=1, I>=1, E>=1");
     if (nseg > kMaxSegments)
@@ -613,7 +663,10 @@ int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* 
     CUtensorMap mx, mwgu, mh, mwd;
     // A boxes hold one CTA's 128 rows; each CTA of a pair holds half of the
     // 256 B rows of a down-projection tile.
-    if (!make_map(&mx, x, rows, d, kTileM, dtype) ||
+    // Gathered form: x holds gather_T token rows and packed row r is token
+    // gather_rows[r] (a one-row box for tile::gather4); otherwise x is packed.
+    if ((gather_rows && gather_T < 1) ||
+        !make_map(&mx, x, gather_rows ? gather_T : rows, d, gather_rows ? 1 : kTileM, dtype) ||
         !make_map(&mwgu, w_gate_up, int64_t(E) * 2 * I, d, kTileN / 2, dtype) ||
         !make_map(&mh, h, rows, I, kTileM, dtype) ||
         !make_map(&mwd, w_down, int64_t(E) * d, I, (cg & 2) ? kTileN / 2 : kTileN, dtype))
@@ -621,9 +674,11 @@ int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* 
     const cudaError_t err =
         dtype == MOE_B200_BF16
             ? launch_ffn<MOE_B200_BF16>(cg, mx, mwgu, mh, mwd, seg_start, seg_expert, nseg, rows, d, I, h, y, st, s,
-                                        dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len)
+                                        dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len, gather_rows,
+                                        gather_T)
             : launch_ffn<MOE_B200_F16>(cg, mx, mwgu, mh, mwd, seg_start, seg_expert, nseg, rows, d, I, h, y, st, s,
-                                       dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len);
+                                       dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len, gather_rows,
+                                       gather_T);
     return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "grouped_swiglu launch");
 }
 }  // namespace moe_b200
@@ -632,5 +687,17 @@ extern "C" int moe_b200_grouped_swiglu(const void* x, const int32_t* seg_start, 
                                        int nseg, int rows, int d, int I, int E, const void* w_gate_up,
                                        const void* w_down, int dtype, void* h, void* y, void* stream) {
     return moe_b200::grouped_swiglu_impl(x, seg_start, seg_expert, nseg, rows, d, I, E, w_gate_up, w_down, dtype,
-                                         h, y, static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr, 1, 0);
+                                         h, y, static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr, 1, 0,
+                                         nullptr, 0);
+}
+
+extern "C" int moe_b200_grouped_swiglu_gather(const void* x_tokens, int T, const int32_t* row_token,
+                                              const int32_t* seg_start, const int32_t* seg_expert, int nseg, int rows,
+                                              int d, int I, int E, const void* w_gate_up, const void* w_down,
+                                              int dtype, void* h, void* y, void* stream) {
+    if (!row_token || T < 1)
+        return moe_b200::fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu_gather: need row_token and T >= 1");
+    return moe_b200::grouped_swiglu_impl(x_tokens, seg_start, seg_expert, nseg, rows, d, I, E, w_gate_up, w_down,
+                                         dtype, h, y, static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr,
+                                         1, 0, row_token, T);
 }

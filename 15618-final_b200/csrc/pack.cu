@@ -28,6 +28,7 @@
 // The reference strategies replaced here re-read each token row once per slot
 // (src/scatter/scatter_csort.cu:57-91, scatter_vec.cu:79-103) and pay a CUB
 // sort or scan plus host-synchronising timers between launches.
+#include <algorithm>
 #include <cstdlib>
 
 #include <cuda_runtime.h>
@@ -388,6 +389,31 @@ pack_rows_bulk_kernel(const uint16_t* __restrict__ emb, const int32_t* __restric
     pdl_launch_dependents();
 }
 
+// Indices only (packed == NULL): perm / packed_weights / slot_pos from the
+// scan, no row copy -- for consumers that gather the rows themselves
+// (moe_b200_grouped_swiglu_gather).  Thread per slot.
+__global__ void __launch_bounds__(256)
+pack_index_kernel(const int32_t* __restrict__ asgn, const float* __restrict__ wts,
+                  const int32_t* __restrict__ rank, const int32_t* __restrict__ expert_start, int64_t TK, int K,
+                  int E, float* __restrict__ packed_w, int32_t* __restrict__ perm, int32_t* __restrict__ slot_pos,
+                  WsHeader* __restrict__ hdr, uint64_t* __restrict__ status, size_t status_words) {
+    pdl_wait_primary();
+    rearm_scan_scratch(hdr, status, status_words);
+    const int64_t nt = int64_t(gridDim.x) * blockDim.x;
+    for (int64_t s = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; s < TK; s += nt) {
+        const int32_t r = rank[s];
+        const int e = __ldg(asgn + s);
+        int32_t pos = -1;
+        if (r >= 0 && e >= 0 && e < E) {
+            pos = expert_start[e] + r;
+            perm[pos] = int32_t(s / K);
+            if (packed_w) packed_w[pos] = __ldg(wts + s);
+        }
+        if (slot_pos) slot_pos[s] = pos;
+    }
+    pdl_launch_dependents();
+}
+
 // Fallback for rows that are not 16-byte multiples / not 16-byte aligned:
 // 2-byte elements, one warp per token.
 __global__ void __launch_bounds__(256)
@@ -462,7 +488,16 @@ cudaError_t launch_pack(const void* emb, const int32_t* asgn, const float* wts, 
 
     cudaError_t err = launch_route_scan(asgn, T, K, E, expert_count, expert_start, ws, stream);
     if (err != cudaSuccess) return err;
-    (void)TK;
+    if (!packed) {
+        cudaLaunchConfig_t cfg = pdl_config(dim3(unsigned(std::min<int64_t>((TK + 255) / 256, int64_t(sm_count()) * 8))),
+                                            dim3(256), 0, stream);
+        cudaLaunchAttribute attr = pdl_attr();
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, pack_index_kernel, asgn, wts, static_cast<const int32_t*>(rank),
+                                  static_cast<const int32_t*>(expert_start), TK, K, E, packed_w, perm, slot_pos,
+                                  hdr, status, words);
+    }
 
     const bool vec = (d % 8 == 0) && (reinterpret_cast<uintptr_t>(emb) % 16 == 0) &&
                      (reinterpret_cast<uintptr_t>(packed) % 16 == 0);

@@ -75,6 +75,9 @@ def lib() -> ctypes.CDLL:
     L.moe_b200_workspace_status.argtypes = [vp, sz, vp, ctypes.POINTER(cint)]
     L.moe_b200_device_status.restype = cint
     L.moe_b200_device_status.argtypes = [vp, ctypes.POINTER(cint)]
+    L.moe_b200_grouped_swiglu_gather.restype = cint
+    L.moe_b200_grouped_swiglu_gather.argtypes = [vp, cint, vp, vp, vp, cint, cint, cint, cint, cint, vp, vp, cint,
+                                                 vp, vp, vp]
     L.moe_b200_grouped_swiglu.restype = cint
     L.moe_b200_grouped_swiglu.argtypes = [vp, vp, vp, cint, cint, cint, cint, cint, vp, vp, cint, vp, vp, vp]
     L.moe_b200_router_weights_bytes.restype = sz
@@ -273,8 +276,9 @@ class Workspace:
 
 
 def pack(emb, asgn, wts, E: int, workspace: Optional[Workspace] = None, out: Optional[PackResult] = None,
-         stream=None) -> PackResult:
-    """Stable pack of emb [T, d] (16-bit) by asgn [T, K] (int32); wts [T, K] fp32."""
+         stream=None, rows: bool = True) -> PackResult:
+    """Stable pack of emb [T, d] (16-bit) by asgn [T, K] (int32); wts [T, K] fp32.
+    rows=False: indices only (packed is None, no row copy)."""
     import torch
     T, d = emb.shape
     K = asgn.shape[1]
@@ -284,7 +288,7 @@ def pack(emb, asgn, wts, E: int, workspace: Optional[Workspace] = None, out: Opt
         workspace = Workspace(T, K, E, device=dev, stream=stream)
     if out is None:
         out = PackResult(
-            packed=torch.empty((TK, d), dtype=emb.dtype, device=dev),
+            packed=torch.empty((TK, d), dtype=emb.dtype, device=dev) if rows else None,
             packed_weights=torch.empty(TK, dtype=torch.float32, device=dev) if wts is not None else None,
             perm=torch.empty(TK, dtype=torch.int32, device=dev),
             expert_count=torch.empty(E, dtype=torch.int32, device=dev),
@@ -328,12 +332,19 @@ def unpermute(y, packed_weights, slot_pos, T: int, K: int, out=None, stream=None
     return out
 
 
-def grouped_swiglu(x, seg_start, w_gate_up, w_down, seg_expert=None, h=None, y=None, stream=None):
+def grouped_swiglu(x, seg_start, w_gate_up, w_down, seg_expert=None, h=None, y=None, stream=None,
+                   row_token=None):
     """Grouped SwiGLU FFN over packed rows x [rows, d] (bf16/fp16).
     seg_start: int32 [nseg + 1] device offsets (e.g. expert_start from pack);
-    w_gate_up [E, 2I, d], w_down [E, d, I].  Returns (h [rows, I], y [rows, d])."""
+    w_gate_up [E, 2I, d], w_down [E, d, I].  Returns (h [rows, I], y [rows, d]).
+    row_token (int32 [rows], e.g. perm from pack): x is then the token matrix
+    [T, d] and packed row r is x[row_token[r]] (gathered, no packed copy)."""
     import torch
-    rows, d = x.shape
+    if row_token is not None:
+        T, d = x.shape
+        rows = row_token.numel()
+    else:
+        rows, d = x.shape
     E, two_i, _ = w_gate_up.shape
     I = two_i // 2
     nseg = seg_start.numel() - 1
@@ -341,6 +352,12 @@ def grouped_swiglu(x, seg_start, w_gate_up, w_down, seg_expert=None, h=None, y=N
         h = torch.empty((rows, I), dtype=x.dtype, device=x.device)
     if y is None:
         y = torch.empty((rows, d), dtype=x.dtype, device=x.device)
+    if row_token is not None:
+        _check(lib().moe_b200_grouped_swiglu_gather(_ptr(x), T, _ptr(row_token), _ptr(seg_start), _ptr(seg_expert),
+                                                    nseg, rows, d, I, E, _ptr(w_gate_up), _ptr(w_down),
+                                                    dtype_code(x.dtype), _ptr(h), _ptr(y), _stream_handle(stream)),
+               "grouped_swiglu_gather")
+        return h, y
     _check(lib().moe_b200_grouped_swiglu(_ptr(x), _ptr(seg_start), _ptr(seg_expert), nseg, rows, d, I, E,
                                          _ptr(w_gate_up), _ptr(w_down), dtype_code(x.dtype), _ptr(h), _ptr(y),
                                          _stream_handle(stream)), "grouped_swiglu")

@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                     help="N>1 expert placement: popularity dealt round-robin over ranks (default) or the "
                          "reference's contiguous ranges")
+    ap.add_argument("--gather", action="store_true",
+                    help="N=1 layer (c5): the gate/up GEMM gathers the token rows (tile::gather4 by perm) and the "
+                         "pack writes indices only (measured slower on B200; default: packed rows)")
     ap.add_argument("--no-router", action="store_true",
                     help="skip the separate router timing (N=1 pack configs)")
     ap.add_argument("--replicate", type=int, default=8,
@@ -77,6 +80,7 @@ def config_json(c, n, l2_note):
         "pipeline": ("pack -> " + ("" if n == 1 else "AllToAllv -> ") + ("grouped SwiGLU FFN" if c.get("I") else "identity")
                      + ("" if n == 1 else " -> AllToAllv") + " -> unpermute"),
         "parallelism": f"ep{n}" if n > 1 else "single-gpu",
+        "rows": c.get("rows", "packed"),
         "placement": c.get("placement", "n/a"),
         "l2": l2_note,
     }
@@ -370,6 +374,9 @@ def gpu_arm(args):
     c = workload(args.config, rank)
     c["name"] = args.config
     c["placement"] = args.placement if world > 1 else "n/a"
+    if "I" in c and world == 1:
+        c["rows"] = ("gathered by the gate/up GEMM from the token rows (tile::gather4 by perm); pack writes "
+                     "indices only" if args.gather else "packed copy")
     layer = "I" in c                       # c5: the full layer with SwiGLU experts
     if layer:
         # the layer's T tokens are split over the ranks (apps/bench_prefill.cu:341)
@@ -404,9 +411,12 @@ def gpu_arm(args):
         local_labels = fep.local_experts
     else:
         local_labels = list(range(lo, hi))
+    # --gather: the gate/up GEMM gathers the token rows itself (TMA
+    # tile::gather4 by perm), so the pack writes indices only
+    gather = layer and world == 1 and args.gather
     with torch.cuda.stream(stream):
         ws = mb.Workspace(T, K, E, device=dev, stream=stream)
-        bufs = mb.pack(emb, asgn, wts, E, workspace=ws, stream=stream)
+        bufs = mb.pack(emb, asgn, wts, E, workspace=ws, stream=stream, rows=not gather)
         out = torch.empty((T, d), dtype=tdtype, device=dev)
         if layer:
             I = c["I"]
@@ -458,13 +468,16 @@ def gpu_arm(args):
         if world > 1:
             x_in, lay = epx.dispatch(bufs.packed, bufs.expert_count, recv_buf)
             seg_start, seg_expert = lay.seg_start, lay.seg_expert
+        elif gather:
+            x_in, seg_start, seg_expert = emb, bufs.expert_start, None
         else:
             x_in, seg_start, seg_expert = bufs.packed, bufs.expert_start, None
         mark(2)
         if layer:
-            n = x_in.shape[0]
+            n = TK if gather else x_in.shape[0]
             _, y = mb.grouped_swiglu(x_in, seg_start, wgu, wdn, seg_expert=seg_expert,
-                                     h=h_buf[:n], y=y_buf[:n], stream=stream)
+                                     h=h_buf[:n], y=y_buf[:n], stream=stream,
+                                     row_token=bufs.perm if gather else None)
         else:
             y = x_in                                  # identity expert
         mark(3)
@@ -544,6 +557,9 @@ def gpu_arm(args):
         kernels = ["route_scan_kernel", "pack_rows_bulk_kernel", "unpermute_bulk_kernel"]
         if layer:
             kernels[2:2] = ["grouped_gemm_kernel<SwiGLU>", "grouped_gemm_kernel<store>"]
+        if gather:
+            kernels = ["route_scan_kernel", "pack_index_kernel", "grouped_gemm_kernel<SwiGLU, gathered rows>",
+                       "grouped_gemm_kernel<store>", "unpermute_bulk_kernel"]
         if fused:
             kernels = ["route_scan_kernel", "ep_publish_kernel", "ep_pack_dispatch_kernel", "ep_receive_kernel"] + \
                 (["grouped_gemm_kernel<SwiGLU>", "grouped_gemm_kernel<store, peer scatter>"] if layer

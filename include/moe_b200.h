@@ -78,7 +78,9 @@ int moe_b200_workspace_init(void* workspace, size_t workspace_bytes, void* strea
  *   asgn           [T, K]    expert of slot (t, k), in [0, E)
  *   wts            [T, K]    routing weight of slot (t, k); may be NULL when
  *                            packed_weights is NULL
- *   packed         [T*K, d]  out: packed[p] = emb[perm[p]]
+ *   packed         [T*K, d]  out: packed[p] = emb[perm[p]]; may be NULL: then
+ *                            only the indices are produced (no row copy, emb
+ *                            unused) for moe_b200_grouped_swiglu_gather
  *   packed_weights [T*K]     out: weight of packed row p (may be NULL)
  *   perm           [T*K]     out: source token of packed row p
  *   expert_count   [E]       out: rows per expert
@@ -190,6 +192,17 @@ int moe_b200_grouped_swiglu(const void* x, const int32_t* seg_start, const int32
                             int nseg, int rows, int d, int I, int E,
                             const void* w_gate_up, const void* w_down, int dtype,
                             void* h, void* y, void* stream);
+
+/* Gathered form (no packed copy of the rows): packed row r is
+ * x_tokens[row_token[r]], row_token = perm from moe_b200_pack (which may then
+ * run with packed = NULL).  The gate/up GEMM fetches its A rows from
+ * x_tokens [T, d] with TMA tile::gather4 loads (4 token rows per load); all
+ * other arguments and results as moe_b200_grouped_swiglu.  The reference's
+ * attempt at the same idea is apps/bench_blocksparse.cu:197-231.           */
+int moe_b200_grouped_swiglu_gather(const void* x_tokens, int T, const int32_t* row_token,
+                                   const int32_t* seg_start, const int32_t* seg_expert, int nseg,
+                                   int rows, int d, int I, int E, const void* w_gate_up,
+                                   const void* w_down, int dtype, void* h, void* y, void* stream);
 
 /* ----------------------------------------------------- expert parallel ---- */
 

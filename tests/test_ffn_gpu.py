@@ -137,3 +137,33 @@ def test_pack_ffn_unpermute_layer_c5_shape(cuda):
     sp = r.slot_pos.view(T, K)[idx].long()
     ref = (w[idx].unsqueeze(-1) * y[sp].float()).sum(1)
     close(out[idx], ref, dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("T,K,E,d,I,dist", [
+    (2048, 4, 16, 256, 128, "zipf"),
+    (1001, 3, 7, 128, 256, "uniform"),     # ragged segments and tile tails
+    (300, 8, 40, 64, 64, "uniform"),       # many small segments, d = one K step
+])
+def test_grouped_swiglu_gather_matches_packed(cuda, dtype, T, K, E, d, I, dist):
+    """Gathered form (A rows fetched from the token matrix with tile::gather4
+    by perm, pack run with packed = NULL) == the packed form, bit for bit."""
+    asgn, wts = routing.gen_routing(T, K, E, dist, seed=T)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(T)
+    x = torch.randn((T, d), generator=g, device="cuda").to(dtype)
+    wgu = (torch.randn((E, 2 * I, d), generator=g, device="cuda") * 0.02).to(dtype)
+    wdn = (torch.randn((E, d, I), generator=g, device="cuda") * 0.02).to(dtype)
+    a = torch.from_numpy(asgn).cuda()
+    w = torch.from_numpy(wts).cuda()
+    full = mb.pack(x, a, w, E)
+    idx = mb.pack(x, a, w, E, rows=False)
+    assert idx.packed is None
+    for f in ("perm", "packed_weights", "expert_count", "expert_start", "slot_pos"):
+        assert torch.equal(getattr(full, f), getattr(idx, f)), f
+    h1, y1 = mb.grouped_swiglu(full.packed, full.expert_start, wgu, wdn)
+    h2, y2 = mb.grouped_swiglu(x, idx.expert_start, wgu, wdn, row_token=idx.perm)
+    torch.cuda.synchronize()
+    assert mb.device_status() == 0
+    assert torch.equal(h1.view(torch.int16), h2.view(torch.int16))
+    assert torch.equal(y1.view(torch.int16), y2.view(torch.int16))
