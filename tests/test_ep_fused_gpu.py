@@ -69,7 +69,7 @@ def run_fused_steps(epx, x, a, w, E, wgu_local, wdn_local, I, identity, steps, d
     return res, ws
 
 
-@pytest.mark.parametrize("replicated", [(), (0, 3, 5)])
+@pytest.mark.parametrize("replicated", [(), (0, 3, 5), tuple(range(16))])  # none / some / every expert
 @pytest.mark.parametrize("identity", [True, False])
 def test_fused_ep_single_rank_matches_single_gpu_layer(cuda, identity, replicated):
     T, K, E, d, I = 2048, 4, 16, 256, 128
