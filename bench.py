@@ -80,7 +80,7 @@ def config_json(c, n, l2_note):
         "pipeline": ("pack -> " + ("" if n == 1 else "AllToAllv -> ") + ("grouped SwiGLU FFN" if c.get("I") else "identity")
                      + ("" if n == 1 else " -> AllToAllv") + " -> unpermute"),
         "parallelism": f"ep{n}" if n > 1 else "single-gpu",
-        "rows": c.get("rows", "packed"),
+        **({"rows": c["rows"]} if "rows" in c else {}),
         "placement": c.get("placement", "n/a"),
         "l2": l2_note,
     }
