@@ -148,6 +148,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
+// After an aborted pipeline, before a producer returns: the most recent load
+// issued into every stage has landed (bounded wait), so no copy is still
+// writing into shared memory when the CTA exits.  `issued` = stage fills
+// issued.  (On the normal path the consumers waited for every fill.)
+__device__ __forceinline__ void drain_stages(uint64_t* full, uint32_t issued, int stages) {
+    for (uint32_t j = issued > uint32_t(stages) ? issued - uint32_t(stages) : 0u; j < issued; ++j)
+        mbar_wait(full + j % uint32_t(stages), (j / uint32_t(stages)) & 1u);
+}
+
 // Bulk (non-tensor) copy global -> shared, completing on an mbarrier.  Both
 // addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,

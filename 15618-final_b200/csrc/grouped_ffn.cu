@@ -359,6 +359,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             }
             if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
         }
+        if (lane == 0 && *abort_flag) drain_stages(ctl->full, it, kStages);
     } else if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
@@ -399,6 +400,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                     }
                 }
             }
+            // the pair's loads complete on the leader's barriers; the final
+            // cluster barrier keeps the peer resident until the leader drained
+            if (crank == 0 && *abort_flag) drain_stages(ctl->full, it, kStages);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer (the pair leader for CG = 2) ----------------

@@ -307,6 +307,7 @@ pack_rows_bulk_kernel(const uint16_t* __restrict__ emb, const int32_t* __restric
     __syncwarp();
     // Prefetch the first rows: inputs only, so no need to wait for the scan.
     const int64_t pre = n < ring ? n : ring;
+    int64_t issued = pre;  // rows 0 .. issued-1 have had their load issued (in order)
     if (lane == 0) {
         for (int64_t i = 0; i < pre; ++i) {
             mbar_arrive_expect_tx(full + i, rowb);
@@ -377,15 +378,18 @@ pack_rows_bulk_kernel(const uint16_t* __restrict__ emb, const int32_t* __restric
                     mbar_arrive_expect_tx(full + js, rowb);
                     bulk_g2s(ring_smem + size_t(js) * rowb, emb + (t0 + j + ring) * d, rowb, full + js);
                 }
+                issued = j + ring + 1;
             }
         }
         e_cur = e_nxt;
         w_cur = w_nxt;
         if (ok) p_cur = position(g + 1, e_cur);
     }
-    // Rows whose refill was skipped above (the last kLag tokens) need no wait;
-    // every store must finish before the shared memory it reads goes away.
+    // Every store must finish before the shared memory it reads goes away,
+    // and (after an abort) every row load still in flight must have landed.
     bulk_wait<0>();
+    if (!ok && lane == 0) drain_stages(full, uint32_t(issued), ring);  // normally every load was waited for
+    __syncwarp();
     pdl_launch_dependents();
 }
 

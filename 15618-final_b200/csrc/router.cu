@@ -261,6 +261,7 @@ route_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__
     } else if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
+            uint32_t issued = 0;
             for (int kb = kb0; kb < kb1; ++kb) {
                 const int j = kb - kb0, st = j % stages;
                 if (!wait_or_abort(&ctl->empty[st], ((j / stages) & 1) ^ 1, abort_flag, dev_status)) break;
@@ -270,7 +271,9 @@ route_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__
                 for (int p = 0; p < P; ++p)
                     tma_load_2d(sa + kRtABytes + p * piece_bytes, &tmap_w, kb * kRtTileK, p * E_pad,
                                 &ctl->full[st]);
+                issued = uint32_t(j + 1);
             }
+            if (*abort_flag) drain_stages(ctl->full, issued, stages);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------

@@ -163,6 +163,7 @@ unpermute_bulk_kernel(const uint16_t* __restrict__ y, const float* __restrict__ 
         float w_cur = fetch_w(p_cur);
         float w_nxt;
         bool ok = true;
+        uint32_t issued = 0;  // stages filled
         for (int64_t g = 0; ok && g * G < n_mine; ++g) {
             const int32_t p_nn = fetch_p(g + 2);
             w_nxt = fetch_w(p_nxt);
@@ -188,11 +189,15 @@ unpermute_bulk_kernel(const uint16_t* __restrict__ y, const float* __restrict__ 
                 if (mine && p_cur >= 0)
                     bulk_g2s(smem + size_t(s) * stage_bytes + size_t(gk) * rowb,
                              y + int64_t(p_cur) * d, rowb, full + s);
+                issued = uint32_t(i + 1);
             }
             p_cur = p_nxt;
             w_cur = w_nxt;
             p_nxt = p_nn;
         }
+        // after an abort, no row copy may still be landing in shared memory
+        // when the CTA exits (normally the consumers waited for every one)
+        if (!ok && lane == 0) drain_stages(full, issued, stages);
     } else {
         const int ctid = tid;  // 0 .. 32*kConsumerWarps-1
         const int nvec = d >> 3;
