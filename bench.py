@@ -545,10 +545,42 @@ def gpu_arm(args):
     if world == 1 and not layer and not args.no_router:
         router = router_leg(mb, c, emb, stream, dev, flusher, args.steps, warm)
 
-    # e2e through the C ABI with pinned host buffers (N = 1, identity expert)
+    # e2e through the C ABI with pinned host buffers: pipelined across steps
+    # for the single-GPU pack path; elsewhere (expert parallel, the layer)
+    # every step is H2D -> step -> D2H on the step's stream, max over ranks
     e2e = None
     if world == 1 and not args.no_e2e and not layer:
         e2e = e2e_leg(mb, c, emb, asgn_np, wts_np, ws, stream, dev, args.steps, warm)
+    elif not args.no_e2e:
+        h_emb = emb.cpu().pin_memory()
+        h_asgn = asgn.cpu().pin_memory()
+        h_wts = wts.cpu().pin_memory()
+        h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        spans = []
+        with torch.cuda.stream(stream):
+            for i in range(warm + args.steps):
+                flusher(i)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                emb.copy_(h_emb, non_blocking=True)
+                asgn.copy_(h_asgn, non_blocking=True)
+                wts.copy_(h_wts, non_blocking=True)
+                step()
+                h_out.copy_(out, non_blocking=True)
+                b.record(stream)
+                if i >= warm:
+                    spans.append((a, b))
+            torch.cuda.synchronize(dev)
+        e2e_ms = torch.tensor([sum(x.elapsed_time(y) for x, y in spans)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+        ms_e2e = float(e2e_ms.item()) / args.steps
+        h2d = T * d * 2 + T * K * 8
+        e2e = {"value": ms_e2e * 1e3 if layer else world * T / (ms_e2e / 1e3),
+               "unit": "us" if layer else UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": T * d * 2,
+               "ms_per_step": ms_e2e,
+               "note": "per rank, every step: inputs H2D from pinned memory, the step, the output D2H, on "
+                       "one stream; max over ranks"}
 
     if rank == 0:
         ms = total_ms / args.steps
