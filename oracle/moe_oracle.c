@@ -16,9 +16,15 @@
  * counterpart in the reference's CPU code (the reference combines only on the
  * GPU with fp32 atomics, apps/bench_e2e.cu:136-152, its FFN has no
  * activation, apps/bench_e2e.cu:289-299, and it routes only on the GPU,
- * apps/bench_e2e.cu:51-130): their parity is "unpinned" and rests on the
- * closed-form identity-expert case, torch fp32 cross-checks and, for the
- * router, a restatement of the reference kernel's float arithmetic (mode 0).
+ * apps/bench_e2e.cu:51-130).  The router and combine restatements are
+ * pinned instead against golden vectors produced by the reference's own GPU
+ * kernels (apps/bench_e2e.cu compiled unchanged into oracle/_ref/libref_gpu.so
+ * by oracle/Makefile and run by tests/golden/make_ref_gpu_golden.py;
+ * checked in tests/test_ref_gpu_golden.py): the gate logits and the combine
+ * at K = 2 (two fp32 atomic adds onto zero commute exactly) bit for bit, the
+ * probabilities, assignments and K = 4 combine within stated bounds.  The
+ * SwiGLU expert stays "unpinned" (no reference counterpart): it rests on
+ * torch fp32 cross-checks.
  *
  * All 16-bit payloads are opaque uint16 words; dtype 0 = fp16, 1 = bf16.
  */
@@ -288,6 +294,45 @@ void oracle_swiglu_expert(const uint16_t* x, const uint16_t* w_gu, const uint16_
         }
     }
     free(xf); free(hf); free(wrow); free(gacc); free(uacc);
+}
+
+/* ------------------------------------------------------------------------ */
+/* The reference's deterministic input fills (include/moe/fp16_host.hpp:22-39):
+ * a 32-bit linear congruential generator s <- s * 1664525 + 1013904223, value
+ * ((s >> 16) / 65536 - 0.5) * 2 * half_range in float, rounded to fp16
+ * (round-to-nearest-even, as __float2half) for the half fill.  Used to
+ * regenerate the inputs of golden vectors made by the reference's GPU code. */
+/* ------------------------------------------------------------------------ */
+static inline float lcg_value(uint32_t* s, float half_range) {
+    *s = *s * 1664525u + 1013904223u;
+    float x = (float)(*s >> 16) / 65536.0f - 0.5f;
+    return x * 2.0f * half_range;
+}
+
+void oracle_fill_random_half(uint16_t* buf, int64_t n, uint32_t seed, float half_range) {
+    uint32_t s = seed;
+    for (int64_t i = 0; i < n; ++i) buf[i] = oracle_f32_to_f16(lcg_value(&s, half_range));
+}
+
+void oracle_fill_random_float(float* buf, int64_t n, uint32_t seed, float half_range) {
+    uint32_t s = seed;
+    for (int64_t i = 0; i < n; ++i) buf[i] = lcg_value(&s, half_range);
+}
+
+/* Gate logits alone, [T, E] fp32: gate_kernel (apps/bench_e2e.cu:52-62) and
+ * the first loop of fused_route_kernel (:101-102), i.e. one float fused
+ * multiply-add per input feature in ascending i (nvcc contracts the
+ * reference's `acc += a * b`).                                              */
+__attribute__((target_clones("fma", "default")))
+void oracle_gate_logits(const uint16_t* emb, const float* w_gate, int T, int d, int E, int dtype,
+                        float* logits) {
+    for (int t = 0; t < T; ++t)
+        for (int e = 0; e < E; ++e) {
+            float acc = 0.f;
+            for (int i = 0; i < d; ++i)
+                acc = fmaf(to_f32(emb[(size_t)t * d + i], dtype), w_gate[(size_t)i * E + e], acc);
+            logits[(size_t)t * E + e] = acc;
+        }
 }
 
 /* ------------------------------------------------------------------------ */

@@ -54,6 +54,12 @@ def lib():
         L.oracle_f32_to_16_array.argtypes = [_P, _P, _L, _I]
         L.oracle_16_to_f32_array.restype = None
         L.oracle_16_to_f32_array.argtypes = [_P, _P, _L, _I]
+        L.oracle_fill_random_half.restype = None
+        L.oracle_fill_random_half.argtypes = [_P, _L, ctypes.c_uint32, ctypes.c_float]
+        L.oracle_fill_random_float.restype = None
+        L.oracle_fill_random_float.argtypes = [_P, _L, ctypes.c_uint32, ctypes.c_float]
+        L.oracle_gate_logits.restype = None
+        L.oracle_gate_logits.argtypes = [_P, _P, _I, _I, _I, _I, _P]
         _lib = L
     return _lib
 
@@ -164,6 +170,31 @@ def route(emb, w_gate, K, dtype, mode=1):
     m = np.empty(T, np.float64)
     lib().oracle_route(_p(emb), _p(w_gate), T, d, E, K, dtype, mode, _p(a), _p(w), _p(m))
     return a, w, m
+
+
+def fill_random_half(n, seed, half_range=0.01):
+    """The reference's LCG fill (include/moe/fp16_host.hpp:22-30), fp16 bits."""
+    out = np.empty(n, np.uint16)
+    lib().oracle_fill_random_half(_p(out), n, seed, half_range)
+    return out
+
+
+def fill_random_float(n, seed, half_range=0.05):
+    """The reference's LCG fill (include/moe/fp16_host.hpp:32-39)."""
+    out = np.empty(n, np.float32)
+    lib().oracle_fill_random_float(_p(out), n, seed, half_range)
+    return out
+
+
+def gate_logits(emb, w_gate, dtype=0):
+    """Gate logits [T, E] in the reference's float order (sequential FMA)."""
+    emb = _c(emb, np.uint16)
+    w_gate = _c(w_gate, np.float32)
+    T, d = emb.shape
+    E = w_gate.shape[1]
+    out = np.empty((T, E), np.float32)
+    lib().oracle_gate_logits(_p(emb), _p(w_gate), T, d, E, dtype, _p(out))
+    return out
 
 
 def f32_to_16(a, dtype):

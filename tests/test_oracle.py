@@ -11,7 +11,10 @@ import pytest
 import oracle
 from conftest import GOLDEN
 
-GOLDEN_FILES = sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
+# packing goldens from the reference's cpu_scatter (make_golden.py); the
+# ref_gpu_* router / combine goldens are checked in test_ref_gpu_golden.py
+GOLDEN_FILES = sorted(glob.glob(os.path.join(GOLDEN, "fixture_*.npz")) +
+                      [os.path.join(GOLDEN, "verify_mini.npz")])
 
 
 def test_golden_files_present():

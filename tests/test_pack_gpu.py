@@ -52,7 +52,9 @@ def assert_same(g, o, E):
         assert g["packed_weights"].tobytes() == o["packed_weights"].tobytes()
 
 
-@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLDEN, "*.npz"))), ids=os.path.basename)
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLDEN, "fixture_*.npz")) +
+                                        [os.path.join(GOLDEN, "verify_mini.npz")]),
+                         ids=os.path.basename)
 def test_pack_matches_reference_golden(cuda, path):
     g = np.load(path)
     E = int(g["E"])

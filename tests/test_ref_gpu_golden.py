@@ -1,0 +1,157 @@
+"""The CPU oracle's router and combine against golden vectors made by the
+reference's OWN GPU kernels (apps/bench_e2e.cu:52-152, compiled unchanged into
+oracle/_ref/libref_gpu.so and run on a B200 by
+tests/golden/make_ref_gpu_golden.py).  This pins the restatements the
+reference has no CPU code for.
+
+Inputs are regenerated with the oracle's restatement of the reference's
+fills (include/moe/fp16_host.hpp:22-39) and checked against the checksums the
+reference's own fill functions produced.  Bounds:
+  - gate logits: bit for bit (both are a sequential fp32 FMA chain);
+  - routing weights: within WREL relative (about 4 ulp): the reference's
+    softmax calls CUDA's expf, the oracle the C library's;
+  - assignments: identical for every token whose reference top-(K+1)
+    probabilities are at least TIE_REL apart (relative, consecutive); closer
+    pairs can swap under those expf ulps (one token in all cases here);
+  - combine: the reference-order restatement (fp32 multiply, then add in
+    ascending packed position) bit for bit at K = 2, where the two atomic adds
+    onto zero commute exactly, and within one fp32 rounding per term at K = 4
+    (atomic order); the product-order restatement (one FMA per slot in
+    ascending k) within one fp16 ulp of the reference's rounded output.
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+ROUTE = sorted(glob.glob(os.path.join(GOLDEN, "ref_gpu_route_*.npz")))
+COMBINE = sorted(glob.glob(os.path.join(GOLDEN, "ref_gpu_combine_*.npz")))
+WREL = 5e-7
+TIE_REL = 1e-6
+
+
+def _name(p):
+    return os.path.basename(p)[len("ref_gpu_"):-len(".npz")]
+
+
+def route_inputs(g):
+    T, d, E = int(g["T"]), int(g["d"]), int(g["E"])
+    emb = oracle.fill_random_half(T * d, int(g["emb_seed"]), float(g["emb_range"])).reshape(T, d)
+    wg = oracle.fill_random_float(d * E, int(g["gate_seed"]), float(g["gate_range"])).reshape(d, E)
+    return emb, wg
+
+
+def combine_inputs(g):
+    T, K, E, d = (int(g[k]) for k in ("T", "K", "E", "d"))
+    y = oracle.fill_random_half(T * K * d, int(g["y_seed"]), float(g["y_range"])).reshape(T * K, d)
+    pw = oracle.fill_random_float(T * K, int(g["w_seed"]), float(g["w_range"]))
+    return y, pw
+
+
+def separated(probs, K):
+    """Tokens whose reference top-(K+1) probabilities are pairwise TIE_REL apart."""
+    top = -np.sort(-probs, axis=1)[:, :K + 1]
+    gaps = (top[:, :-1] - top[:, 1:]) / top[:, :-1]
+    return gaps.min(axis=1) >= TIE_REL
+
+
+def test_goldens_present():
+    assert len(ROUTE) == 5 and len(COMBINE) == 2
+
+
+def test_fill_restatement_matches_reference_fill():
+    """Where the reference-built library is present, compare the fills directly."""
+    import ctypes
+    so = os.path.join(os.path.dirname(GOLDEN), "..", "oracle", "_ref", "libref_gpu.so")
+    if not os.path.exists(so):
+        pytest.skip("oracle/_ref/libref_gpu.so not built")
+    L = ctypes.CDLL(so)
+    for fn in (L.ref_fill_random_half, L.ref_fill_random_float):
+        fn.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32, ctypes.c_float]
+        fn.restype = None
+    for n, seed, hr in [(100000, 1, 0.01), (50000, 7, 1.0), (1000, 123456789, 3.0)]:
+        h = np.empty(n, np.uint16)
+        f = np.empty(n, np.float32)
+        L.ref_fill_random_half(h.ctypes.data, n, seed, hr)
+        L.ref_fill_random_float(f.ctypes.data, n, seed, hr)
+        assert np.array_equal(h, oracle.fill_random_half(n, seed, hr))
+        assert np.array_equal(f.view(np.uint32), oracle.fill_random_float(n, seed, hr).view(np.uint32))
+
+
+@pytest.mark.parametrize("path", ROUTE, ids=_name)
+def test_route_inputs_regenerate(path):
+    g = np.load(path)
+    emb, wg = route_inputs(g)
+    assert emb.astype(np.int64).sum() == int(g["emb_sum"])
+    assert wg.view(np.uint32).astype(np.int64).sum() == int(g["gate_sum"])
+
+
+@pytest.mark.parametrize("path", ROUTE, ids=_name)
+def test_gate_logits_bit_exact(path):
+    g = np.load(path)
+    emb, wg = route_inputs(g)
+    assert np.array_equal(oracle.gate_logits(emb, wg).view(np.uint32), g["logits"].view(np.uint32))
+
+
+@pytest.mark.parametrize("path", ROUTE, ids=_name)
+def test_reference_routers_agree(path):
+    """fused_route_kernel and gate -> softmax -> topk give the same outputs."""
+    g = np.load(path)
+    assert np.array_equal(g["fused_asgn"], g["naive_asgn"])
+    assert np.array_equal(g["fused_wts"].view(np.uint32), g["naive_wts"].view(np.uint32))
+
+
+@pytest.mark.parametrize("path", ROUTE, ids=_name)
+def test_route_mode0_matches_reference_gpu(path):
+    g = np.load(path)
+    K = int(g["K"])
+    emb, wg = route_inputs(g)
+    a0, w0, _ = oracle.route(emb, wg, K, 0, mode=0)
+    fa, fw = g["fused_asgn"], g["fused_wts"]
+    sep = separated(g["probs"], K)
+    assert sep.mean() > 0.98
+    assert np.array_equal(a0[sep], fa[sep])
+    same = (a0 == fa).all(axis=1)
+    assert same.mean() > 0.98
+    np.testing.assert_allclose(w0[same], fw[same], rtol=WREL, atol=0)
+    # the double-precision oracle agrees at the same separation
+    a1, w1, _ = oracle.route(emb, wg, K, 0, mode=1)
+    assert np.array_equal(a1[sep], fa[sep])
+
+
+@pytest.mark.parametrize("path", COMBINE, ids=_name)
+def test_combine_inputs_regenerate(path):
+    g = np.load(path)
+    y, pw = combine_inputs(g)
+    assert y.astype(np.int64).sum() == int(g["y_sum"])
+    assert np.array_equal(pw.view(np.uint32), g["packed_weights"].view(np.uint32))
+
+
+@pytest.mark.parametrize("path", COMBINE, ids=_name)
+def test_combine_matches_reference_gpu(path):
+    g = np.load(path)
+    T, K, E = int(g["T"]), int(g["K"]), int(g["E"])
+    y, pw = combine_inputs(g)
+    perm = g["perm"]
+    o32 = oracle.combine_by_perm(y, pw, perm, T, 0)
+    if K <= 2:
+        assert np.array_equal(o32.view(np.uint32), g["out32"].view(np.uint32))
+    else:
+        # each of the K terms is rounded once in either order
+        bound = K * np.finfo(np.float32).eps * np.abs(o32).max()
+        assert np.abs(o32 - g["out32"]).max() <= bound
+    assert np.array_equal(oracle.f32_to_16(g["out32"], 0), g["out16"])  # f32_to_f16_kernel = RNE
+
+    # the product's order (an FMA per slot in ascending k) on the same layout
+    t = np.arange(T)[:, None]
+    k = np.arange(K)[None, :]
+    asgn = ((7 * t + 13 * k) % E).astype(np.int32)
+    r = oracle.scatter(np.zeros((T, 1), np.uint16), asgn, np.zeros((T, K), np.float32), E)
+    assert np.array_equal(r["perm"], perm)
+    c = oracle.combine(y, pw, r["slot_pos"], T, K, 0)
+    ulps = np.abs(c.astype(np.int32) - g["out16"].astype(np.int32))
+    assert ulps.max() <= 1
