@@ -6,15 +6,19 @@ One step = one pass of the hot path over one batch:
   N = 1   pack (route_scan + pack_rows) -> identity expert -> unpermute, on the
           single-B200 workload (config c2: T=8192, d=2048 fp16, E=60, K=4,
           Zipf s=1.2 routing).
-  N > 1   (torchrun, one rank per GPU, NCCL) each rank packs its own T=8192
-          tokens, AllToAllv-dispatches the packed rows to the expert-owning
-          ranks, applies the identity expert, AllToAllv-combines them back and
-          unpermutes: weak scaling, value = all ranks' tokens / max-rank time.
+  N > 1   (torchrun, one rank per GPU) each rank packs its own T=8192 tokens
+          and stores the packed rows straight into the expert-owning ranks'
+          receive buffers over NVLink (CUDA IPC peer memory; `--ep nccl`
+          selects the AllToAllv variant), applies the identity expert, returns
+          the rows the same way and unpermutes: weak scaling, value = all
+          ranks' tokens / max-rank time.
 
 Prints ONE JSON line on rank 0.  `value` is device-timed (CUDA events on the
 launching stream, inputs resident in HBM, L2 flushed by a 256 MiB write + a
 256 MiB read before every step); `e2e` is the same metric through the C ABI with pinned host
-buffers and the host<->device copies inside the timed region.
+buffers and the host<->device copies inside the timed region.  `clocks`: the
+SM clock and clock-event reasons read through NVML every 2 ms during the
+timed region (nvidia-smi -lms 200 when NVML is unavailable).
 """
 from __future__ import annotations
 
@@ -129,16 +133,64 @@ def committed_traffic(kernel, workload_name):
 # --------------------------------------------------------------- clocks ----
 
 class ClockSampler:
+    """Samples one GPU's SM clock and clock-event (throttle) reasons while the
+    timed region runs.  Reads NVML (the library nvidia-smi queries) every 2 ms
+    from a thread, so even a timed region of a few milliseconds gets samples;
+    falls back to `nvidia-smi -lms 200` when NVML cannot be opened.  Only
+    reads: no clock, power or other setting is touched."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "HwSlowdown", 0x8), ("hw_thermal_slowdown", "HwThermalSlowdown", 0x40),
+               ("sw_thermal_slowdown", "SwThermalSlowdown", 0x20), ("sw_power_cap", "SwPowerCap", 0x4))
 
-    def __init__(self, gpu_index):
+    def __init__(self, gpu_index, uuid=None):
         self.gpu = gpu_index
+        self.uuid = uuid
         self.proc = None
+        self.nvml = None
         self.lines = []
+        self.samples = []            # (sm MHz, reason bit mask) from NVML
+        self.smax = None
+
+    def _open_nvml(self):
+        import pynvml
+        pynvml.nvmlInit()
+        h = None
+        if self.uuid:
+            u = str(self.uuid)
+            for cand in (u, "GPU-" + u):
+                try:
+                    h = pynvml.nvmlDeviceGetHandleByUUID(cand)
+                    break
+                except Exception:
+                    h = None
+        if h is None:
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+        get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        self.smax = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        self.nvml = (pynvml, h, get_reasons)
+
+    def _poll_nvml(self):
+        pynvml, h, get_reasons = self.nvml
+        while not self.stop.is_set():
+            try:
+                self.samples.append((float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)),
+                                     int(get_reasons(h))))
+            except Exception:
+                pass
+            self.stop.wait(0.002)
 
     def __enter__(self):
+        self.stop = threading.Event()
+        try:
+            self._open_nvml()
+            self.thread = threading.Thread(target=self._poll_nvml, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
@@ -155,6 +207,13 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *a):
+        if self.nvml:
+            self.stop.set()
+            self.thread.join(timeout=5)
+            try:
+                self.nvml[0].nvmlShutdown()
+            except Exception:
+                pass
         if self.proc:
             time.sleep(0.25)
             self.proc.terminate()
@@ -164,8 +223,18 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        if self.samples:
+            import pynvml
+            reasons = set()
+            for name, suffix, bit in self.REASONS:
+                mask = getattr(pynvml, "nvmlClocksEventReason" + suffix, bit)
+                if any(r & mask for _, r in self.samples):
+                    reasons.add(name)
+            return {"sm_mhz": statistics.median(c for c, _ in self.samples), "sm_max_mhz": self.smax,
+                    "sm_min_mhz": min(c for c, _ in self.samples), "reasons": sorted(reasons),
+                    "samples": len(self.samples), "source": "NVML, every 2 ms during the timed region"}
         if not self.lines:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
@@ -181,7 +250,7 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi -lms 200"}
 
 
 # ------------------------------------------------------------- L2 flush ----
@@ -506,7 +575,7 @@ def gpu_arm(args):
             dist.barrier()
         torch.cuda.synchronize(dev)
         rec = []
-        with ClockSampler(local) as clk:
+        with ClockSampler(local, getattr(torch.cuda.get_device_properties(dev), "uuid", None)) as clk:
             for i in range(args.steps):
                 flusher(i)
                 rec.append(step())
