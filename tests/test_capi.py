@@ -110,3 +110,40 @@ def test_router_rejects_bad_arguments_on_host():
     assert L.moe_b200_route(p + 8, 16, 64, 16, 2, mb.F16, p, p, p, None) == mb.ERR_INVALID_ARG  # alignment
     assert L.moe_b200_route(p, 0, 64, 16, 2, mb.F16, p, p, p, None) == mb.OK  # empty: no-op
     assert L.moe_b200_router_prepare(None, 64, 16, mb.F16, p, None) == mb.ERR_INVALID_ARG
+
+
+def test_ep_create_rejects_bad_arguments_on_host():
+    """Expert-parallel context creation validates its geometry before any
+    device call (the reference asserts E % N == 0 instead,
+    apps/bench_prefill.cu:361; uneven contiguous ranges are accepted here)."""
+    import ctypes
+    L = mb.lib()
+    ctx = ctypes.c_void_p()
+
+    def create(N=2, rank=0, E=8, K=2, d=64, max_tokens=16, first=None, timeout_ms=100):
+        first = list(range(0, E + 1, E // N)) if first is None else first
+        arr = (ctypes.c_int32 * len(first))(*first)
+        return L.moe_b200_ep_create(N, rank, E, K, d, max_tokens, arr, timeout_ms, ctypes.byref(ctx))
+
+    assert create(N=0, first=[0, 8]) == mb.ERR_INVALID_ARG
+    assert create(rank=2) == mb.ERR_INVALID_ARG
+    assert create(rank=-1) == mb.ERR_INVALID_ARG
+    assert create(K=0) == mb.ERR_INVALID_ARG
+    assert create(K=33) == mb.ERR_INVALID_ARG
+    assert create(d=60) == mb.ERR_INVALID_ARG
+    assert create(max_tokens=0) == mb.ERR_INVALID_ARG
+    assert create(timeout_ms=0) == mb.ERR_INVALID_ARG
+    assert create(N=4, E=2, first=[0, 1, 2, 2, 2]) == mb.ERR_INVALID_ARG        # E < N
+    assert create(first=[0, 4, 7]) == mb.ERR_INVALID_ARG                        # does not end at E
+    assert create(first=[1, 4, 8]) == mb.ERR_INVALID_ARG                        # does not start at 0
+    assert create(first=[0, 0, 8]) == mb.ERR_INVALID_ARG                        # a rank owns nothing
+    assert create(E=2048, first=[0, 1024, 2048]) == mb.ERR_UNSUPPORTED
+    assert b"ep_create" in L.moe_b200_last_error()
+    assert not ctx.value
+
+
+def test_ep_calls_without_a_context():
+    L = mb.lib()
+    assert L.moe_b200_ep_set_replicated(None, None, 0) == mb.ERR_INVALID_ARG
+    assert L.moe_b200_ep_local_experts(None, None) == -1
+    assert L.moe_b200_ep_destroy(None) == mb.OK
