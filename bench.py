@@ -76,13 +76,19 @@ def workload(cfg_name, rank=0):
 
 
 def config_json(c, n, l2_note):
+    xfer = {"fused": "peer-store exchange over NVLink", "nccl": "NCCL AllToAllv"}.get(c.get("ep", "fused"))
+    if xfer is None:            # the CPU reference: one host, nothing to exchange
+        n_pipe = 1
+    else:
+        n_pipe = n
     return {
         "workload": f"{c['name']}: T={c['T']} per GPU, d={c['d']} {c['dtype']}, E={c['E']}, "
                     f"K={c['K']}, {c['dist']} routing" + (" s=1.2" if c["dist"] == "zipf" else ""),
         "T_per_gpu": c["T"], "d": c["d"], "E": c["E"], "K": c["K"], "routing": c["dist"],
         "expert": f"SwiGLU FFN, I={c['I']}" if c.get("I") else "identity",
-        "pipeline": ("pack -> " + ("" if n == 1 else "AllToAllv -> ") + ("grouped SwiGLU FFN" if c.get("I") else "identity")
-                     + ("" if n == 1 else " -> AllToAllv") + " -> unpermute"),
+        "pipeline": ("pack -> " + ("" if n_pipe == 1 else xfer + " -> ")
+                     + ("grouped SwiGLU FFN" if c.get("I") else "identity")
+                     + ("" if n_pipe == 1 else " -> " + xfer) + " -> unpermute"),
         "parallelism": f"ep{n}" if n > 1 else "single-gpu",
         **({"rows": c["rows"]} if "rows" in c else {}),
         "placement": c.get("placement", "n/a"),
@@ -364,6 +370,8 @@ def reference_arm(args):
         return
     c = workload(args.config)
     c["name"] = args.config
+    c["ep"] = "host"
+    c["placement"] = "n/a (every rank's tokens on the host cores)" if args.gpus > 1 else "n/a"
     cores = host_cores()
     T_sample = min(c["T"], 2048)
     warm = max(args.warmup, 3)
@@ -373,7 +381,7 @@ def reference_arm(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": steps, "warmup": min(warm, 3), "ms_per_step": per_step * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp16 rows, fp32 combine", "data": "synthetic",
-        "config": config_json(c, 1, "n/a (host memory)"),
+        "config": config_json(c, args.gpus, "n/a (host memory)"),
         "cpu_baseline": {
             "value": value, "unit": UNIT, "cores": cores, "kind": kind,
             "sample": f"{cores} host threads, each packing + combining its own {T_sample}-token slice of the "
@@ -443,6 +451,7 @@ def gpu_arm(args):
     c = workload(args.config, rank)
     c["name"] = args.config
     c["placement"] = args.placement if world > 1 else "n/a"
+    c["ep"] = args.ep
     if "I" in c and world == 1:
         c["rows"] = ("gathered by the gate/up GEMM from the token rows (tile::gather4 by perm); pack writes "
                      "indices only" if args.gather else "packed copy")
