@@ -456,6 +456,7 @@ def gpu_arm(args):
         c["rows"] = ("gathered by the gate/up GEMM from the token rows (tile::gather4 by perm); pack writes "
                      "indices only" if args.gather else "packed copy")
     layer = "I" in c                       # c5: the full layer with SwiGLU experts
+    T_glob = c["T"]
     if layer:
         # the layer's T tokens are split over the ranks (apps/bench_prefill.cu:341)
         if c["T"] % world:
@@ -464,13 +465,22 @@ def gpu_arm(args):
     T, K, E, d = c["T"], c["K"], c["E"], c["d"]
     TK = T * K
     tdtype = getattr(torch, c["dtype"])
-    asgn_np, wts_np = routing.gen_routing(T, K, E, c["dist"], c["seed"])
+    if layer:
+        # every rank takes its slice of ONE global batch, so the layer's
+        # outputs (and the checksum below) are the same for every N
+        seed0 = routing.CONFIGS[args.config]["seed"]
+        a_g, w_g = routing.gen_routing(T_glob, K, E, c["dist"], seed0)
+        asgn_np = np.ascontiguousarray(a_g[rank * T:(rank + 1) * T])
+        wts_np = np.ascontiguousarray(w_g[rank * T:(rank + 1) * T])
+        emb = routing.gen_rows(T_glob, d, c["dtype"], seed0, device=dev)[rank * T:(rank + 1) * T].contiguous()
+    else:
+        asgn_np, wts_np = routing.gen_routing(T, K, E, c["dist"], c["seed"])
+        emb = routing.gen_rows(T, d, c["dtype"], c["seed"], device=dev)
     label = list(range(E))
     if world > 1 and args.placement == "balanced":
         label = ep.balanced_labels(E, world)
         asgn_np = np.asarray(label, dtype=np.int32)[asgn_np]
     orig_of = {l: e for e, l in enumerate(label)}
-    emb = routing.gen_rows(T, d, c["dtype"], c["seed"], device=dev)
     asgn = torch.from_numpy(asgn_np).to(dev)
     wts = torch.from_numpy(wts_np).to(dev)
 
@@ -609,11 +619,16 @@ def gpu_arm(args):
     total_ms = sum(step_ms)
     stage = torch.tensor([statistics.fmean(pack_ms), statistics.fmean(mid_ms), statistics.fmean(expert_ms),
                           statistics.fmean(unperm_ms)], dtype=torch.float64, device=dev)
+    # L2 norm of the last step's output over all tokens of all ranks, the
+    # reference's multi-GPU consistency check (apps/bench_prefill.cu:955-972)
+    sumsq = out.float().square().sum(dtype=torch.float64).reshape(1)
     if world > 1:
         t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
         dist.all_reduce(stage, op=dist.ReduceOp.MAX)
+        dist.all_reduce(sumsq, op=dist.ReduceOp.SUM)
+    out_l2 = float(sumsq.item()) ** 0.5
     mean_pack, mean_mid, mean_expert, mean_unperm = stage.tolist()
 
     # The router (gate GEMM + softmax + top-K) on the same tokens, timed alone
@@ -697,6 +712,11 @@ def gpu_arm(args):
             "gpu_launches": len(kernels) * args.steps + (args.steps if world > 1 and not fused else 0),
             "kernels_per_step": kernels + (["ep_layout_kernel"] if world > 1 and not fused else []),
             "clocks": clk.summary(),
+            "checksum": {"output_l2": out_l2,
+                         "note": ("L2 norm of the layer output over the whole batch (all ranks); every rank "
+                                  "holds a slice of one global batch, so it is the same for every N")
+                         if layer else ("L2 norm of the output over all ranks' tokens (each rank its own "
+                                        "seeded batch, so it grows with N)")},
         }
         if layer:
             I = c["I"]
