@@ -1,0 +1,45 @@
+"""The benchmark's JSON contract, checked on the CPU through the reference
+arm (`bench.py --impl reference`, the reference's own cpu_scatter + the
+combine restatement on the host cores): one JSON line with the keys the
+harness reads, at N = 1 and, under torchrun with two CPU ranks, only
+rank 0 printing."""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+KEYS = {"impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+        "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"}
+
+
+def run(args, env=None):
+    r = subprocess.run([sys.executable] + args, cwd=ROOT, capture_output=True, text=True, timeout=600,
+                       env=env)
+    assert r.returncode == 0, r.stderr[-2000:]
+    return [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+
+
+def test_reference_arm_line():
+    lines = run(["bench.py", "--impl", "reference", "--steps", "1", "--warmup", "3"])
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert KEYS <= set(d)
+    assert d["impl"] == "reference" and d["n_gpus"] == 1 and d["warmup"] >= 3
+    assert d["value"] > 0 and d["unit"] == "tokens/s" and d["higher_is_better"] is True
+    assert d["config"]["workload"].startswith("c2")
+    cb = d["cpu_baseline"]
+    assert cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["value"] == d["value"]
+    assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_prints_on_rank_zero_only():
+    env = dict(os.environ, MASTER_ADDR="127.0.0.1")
+    lines = run(["-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2", "--master-addr",
+                 "127.0.0.1", "--master-port", "29581", "bench.py", "--impl", "reference", "--gpus", "2",
+                 "--steps", "1", "--warmup", "3"], env=env)
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["n_gpus"] == 2 and d["config"]["parallelism"] == "ep2"
