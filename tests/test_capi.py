@@ -147,3 +147,25 @@ def test_ep_calls_without_a_context():
     assert L.moe_b200_ep_set_replicated(None, None, 0) == mb.ERR_INVALID_ARG
     assert L.moe_b200_ep_local_experts(None, None) == -1
     assert L.moe_b200_ep_destroy(None) == mb.OK
+
+
+def test_grouped_swiglu_rejects_bad_arguments_on_host():
+    L = mb.lib()
+    p = 0x2000
+
+    def ffn(x=p, seg=p, nseg=4, rows=64, d=64, I=32, E=4, dtype=mb.BF16, h=p, y=p):
+        return L.moe_b200_grouped_swiglu(x, seg, None, nseg, rows, d, I, E, p, p, dtype, h, y, None)
+
+    assert ffn(nseg=0) == mb.ERR_INVALID_ARG
+    assert ffn(rows=-1) == mb.ERR_INVALID_ARG
+    assert ffn(nseg=1025) == mb.ERR_UNSUPPORTED
+    assert ffn(dtype=7) == mb.ERR_INVALID_ARG
+    assert ffn(d=72) == mb.ERR_UNSUPPORTED           # d % 16
+    assert ffn(I=40) == mb.ERR_UNSUPPORTED           # I % 16
+    assert ffn(x=None) == mb.ERR_INVALID_ARG
+    assert ffn(y=None) == mb.ERR_INVALID_ARG
+    assert ffn(h=p + 8) == mb.ERR_INVALID_ARG        # 16-byte alignment
+    assert ffn(rows=0) == mb.OK                      # empty: no-op
+    assert L.moe_b200_grouped_swiglu_gather(p, 0, p, p, None, 4, 64, 64, 32, 4, p, p, mb.BF16, p, p,
+                                            None) == mb.ERR_INVALID_ARG
+    assert b"grouped_swiglu" in L.moe_b200_last_error()
