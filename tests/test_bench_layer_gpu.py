@@ -18,7 +18,9 @@ BIN = os.path.join(ROOT, "15618-final_b200", "_build", "bench_layer")
 @pytest.mark.parametrize("dtype", ["bf16", "fp16"])
 @pytest.mark.parametrize("T,d,E,K,I", [(1000, 256, 16, 4, 128), (333, 512, 60, 2, 64)])
 def test_bench_layer_checks_pass(cuda, dtype, T, d, E, K, I):
-    assert os.path.exists(BIN), "build the harness first (make -C 15618-final_b200)"
+    if not os.path.exists(BIN):
+        subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "15618-final_b200"), "apps"], check=True,
+                       timeout=600)
     r = subprocess.run([BIN, "--T", str(T), "--d", str(d), "--E", str(E), "--K", str(K), "--I", str(I),
                         "--dtype", dtype, "--iters", "2", "--warmup", "1"],
                        capture_output=True, text=True, timeout=300)
