@@ -35,10 +35,17 @@ def test_reference_arm_line():
                         "d2h_bytes_per_step": 0}
 
 
+def _free_port():
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
 def test_reference_arm_prints_on_rank_zero_only():
     env = dict(os.environ, MASTER_ADDR="127.0.0.1")
     lines = run(["-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2", "--master-addr",
-                 "127.0.0.1", "--master-port", "29581", "bench.py", "--impl", "reference", "--gpus", "2",
+                 "127.0.0.1", "--master-port", str(_free_port()), "bench.py", "--impl", "reference", "--gpus", "2",
                  "--steps", "1", "--warmup", "3"], env=env)
     assert len(lines) == 1
     d = json.loads(lines[0])
