@@ -198,3 +198,32 @@ def test_route_oracle_hand_example():
     prob /= prob.sum(1, keepdims=True)
     assert a.tolist() == [[3, 0], [1, 2]]
     np.testing.assert_allclose(p, np.sort(prob, 1)[:, ::-1][:, :2], rtol=1e-6)
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="reference CPU oracle not built")
+def test_oracle_matches_reference_binary_property():
+    """Property form of the pin: for any small shape and any assignment
+    (repeats within a token allowed, as cpu_scatter accepts them), the
+    restatement and the reference binary produce the same bytes and both
+    pass the reference's own invariant checker."""
+    from hypothesis import given, settings, strategies as st
+
+    @settings(max_examples=150, deadline=None, derandomize=True)
+    @given(st.integers(1, 40), st.integers(1, 6), st.integers(1, 12), st.sampled_from([8, 16, 24]),
+           st.integers(0, 2**31 - 1))
+    def check(T, K, E, d, seed):
+        rng = np.random.default_rng(seed)
+        emb = rng.integers(0, 65536, size=(T, d), dtype=np.uint16)
+        asgn = rng.integers(0, E, size=(T, K), dtype=np.int32)
+        wts = rng.random((T, K), dtype=np.float32)
+        a = oracle.scatter(emb, asgn, wts, E)
+        b = oracle.ref_scatter(emb, asgn, wts, E)
+        for key in ("packed", "packed_weights", "perm", "expert_count"):
+            assert a[key].tobytes() == b[key].tobytes(), key
+        assert np.array_equal(a["expert_start"][:E], b["expert_start"]) and a["expert_start"][E] == T * K
+        assert oracle.ref_verify(emb, asgn, wts, a["packed"], a["packed_weights"], a["expert_start"],
+                                 a["expert_count"], a["perm"], E)
+        assert oracle.verify(emb, asgn, wts, a["packed"], a["packed_weights"], a["expert_start"],
+                             a["expert_count"], a["perm"], E) == 0
+
+    check()
