@@ -50,3 +50,26 @@ def test_reference_arm_prints_on_rank_zero_only():
     assert len(lines) == 1
     d = json.loads(lines[0])
     assert d["n_gpus"] == 2 and d["config"]["parallelism"] == "ep2"
+
+
+def test_clock_summary_names_reasons_from_nvml_bits():
+    """ClockSampler.summary() on injected samples (no GPU, no NVML calls):
+    median SM clock, and every clock-event reason bit seen during the region."""
+    sys.path.insert(0, ROOT)
+    import pynvml
+    import bench
+    c = bench.ClockSampler(0)
+    c.smax = 1965.0
+    cap, slow = pynvml.nvmlClocksEventReasonSwPowerCap, pynvml.nvmlClocksEventReasonHwSlowdown
+    c.samples = [(1965.0, 0), (1800.0, cap), (1965.0, 0), (1500.0, cap | slow)]
+    s = c.summary()
+    assert s["sm_mhz"] == 1882.5 and s["sm_min_mhz"] == 1500.0 and s["samples"] == 4
+    assert s["reasons"] == ["hw_slowdown", "sw_power_cap"]
+    c.samples = [(1965.0, pynvml.nvmlClocksEventReasonGpuIdle)]
+    assert c.summary()["reasons"] == []
+    # nvidia-smi fallback lines
+    c = bench.ClockSampler(0)
+    c.lines = ["0, 1965, 1965, 700.1, 0x0, Not Active, Not Active, Not Active, Active",
+               "0, 1950, 1965, 710.0, 0x0, Not Active, Not Active, Not Active, Not Active"]
+    s = c.summary()
+    assert s["sm_mhz"] == 1957.5 and s["sm_max_mhz"] == 1965.0 and s["reasons"] == ["sw_power_cap"]
