@@ -14,7 +14,8 @@ cudaError_t launch_pack(const void* emb, const int32_t* asgn, const float* wts, 
                         int32_t* expert_count, int32_t* expert_start, int32_t* slot_pos,
                         void* ws, cudaStream_t stream);
 cudaError_t launch_unpermute(const void* y, const float* packed_w, const int32_t* slot_pos,
-                             int T, int K, int d, int dtype, void* out, cudaStream_t stream);
+                             int T, int K, int d, int dtype, void* out, cudaStream_t stream,
+                             const EpWait* wait);
 
 static thread_local char g_last_error[512];
 
@@ -135,7 +136,7 @@ int moe_b200_unpermute(const void* y, const float* packed_weights, const int32_t
     if (!y || !packed_weights || !slot_pos || !out)
         return fail(MOE_B200_ERR_INVALID_ARG, "unpermute: null pointer");
     cudaError_t err = launch_unpermute(y, packed_weights, slot_pos, T, K, d, dtype, out,
-                                       static_cast<cudaStream_t>(stream));
+                                       static_cast<cudaStream_t>(stream), nullptr);
     return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "unpermute launch");
 }
 

@@ -190,6 +190,72 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 uint32_t* device_status_word();  // status.cu
 
+// ------------------------------------------- expert-parallel flag words ----
+// System-scope acquire / release on epoch words that other GPUs read or write
+// over NVLink (CUDA IPC mappings).
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Orders this thread's earlier generic-proxy accesses (e.g. an acquire of a
+// peer's flag) before its later async-proxy (cp.async.bulk) global accesses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Count publication folded into the route/scan kernel (expert parallel):
+// the tile that finishes the scan writes the final expert counts into row
+// `rank` of every rank's counts inbox and raises every rank's counts flag
+// [rank] to `epoch`.  peer == nullptr: no publication (single GPU).
+struct EpPublish {
+    char* const* peer;  // device array: every rank's region base, this address space
+    size_t off_inbox, off_flag;
+    int rank, nranks;
+    uint64_t epoch;
+};
+
+// "Last CTA raises the flags": every CTA of a grid that stored rows into
+// peers' buffers counts itself done in `counter`; the last one raises flag
+// word [rank] at `flag_off` of every rank's region to `epoch`, unless some
+// CTA reported a failure in `failed` (then no flag is raised and the peers'
+// bounded waits time out and report it themselves).  peer == nullptr: off.
+struct EpSignal {
+    char* const* peer;
+    size_t flag_off;
+    uint32_t* counter;  // [0]: CTAs done, [1]: failure mark; both start and end at 0
+    int rank, nranks;
+    uint64_t epoch;
+};
+
+// Called by one thread per CTA after the CTA's peer stores were fenced
+// system-wide and the CTA synchronised.
+__device__ __forceinline__ void ep_signal_done(const EpSignal& sig, bool cta_failed) {
+    if (cta_failed) atomicOr(sig.counter + 1, 1u);
+    __threadfence();
+    const uint32_t prev = atomicAdd(sig.counter, 1u);
+    if (prev != gridDim.x * gridDim.y * gridDim.z - 1) return;
+    __threadfence();
+    const bool any_failed = atomicExch(sig.counter + 1, 0u) != 0u;
+    sig.counter[0] = 0;
+    if (any_failed) return;
+    __threadfence_system();
+    for (int p = 0; p < sig.nranks; ++p)
+        st_release_sys(reinterpret_cast<uint64_t*>(sig.peer[p] + sig.flag_off) + sig.rank, sig.epoch);
+}
+
+// Bounded wait (in the kernel that consumes the peers' rows) for flag words
+// [0, n) at `flags` to reach `epoch`.  flags == nullptr: no wait.
+struct EpWait {
+    const uint64_t* flags;
+    int n;
+    uint64_t epoch;
+    uint64_t timeout_ns;
+};
+
 // After the route/scan grid has finished (PDL wait done): re-zero its ticket
 // and look-back words so the workspace is ready for the next call.
 __device__ __forceinline__ void rearm_scan_scratch(WsHeader* hdr, uint64_t* status, size_t words) {

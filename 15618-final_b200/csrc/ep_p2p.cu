@@ -9,23 +9,24 @@
 //                              sender-major then local-expert-major
 //   back   [max_tokens * K][d] this rank's rows after their expert, in its
 //                              own packed order
-// One step (epoch e, the same on all ranks; epochs only grow, so no word is
-// ever reset):
-//   1. route_scan (pack.cu) -> local counts / starts / ranks
-//   2. ep_publish_kernel: write the counts into every peer's inbox, raise
+// One step (epoch e, the same on all ranks; epochs only grow, so no flag is
+// ever reset), five launches on one stream for the identity expert:
+//   1. route_scan (pack.cu): local counts / starts / ranks; the tile that
+//      finishes the scan writes the counts into every peer's inbox and raises
 //      counts flag = e on every peer (system-scope release)
-//   3. ep_pack_dispatch_kernel: wait for all counts, then every token row is
+//   2. ep_pack_dispatch_kernel: wait for all counts, then every token row is
 //      read once and stored K times straight into the receive buffer of the
 //      rank owning each slot's expert (NVLink stores); the last CTA raises
 //      data flag = e on every peer
-//   4. ep_receive_kernel (receiver): wait for all data flags, build the
+//   3. ep_receive_kernel (receiver): wait for all data flags, build the
 //      segment table of the receive buffer + each segment's return address
-//   5. the expert: grouped SwiGLU whose down-GEMM epilogue stores every row
+//   4. the expert: grouped SwiGLU whose down-GEMM epilogue stores every row
 //      straight into the sender's back buffer (grouped_ffn.cu scatter mode),
-//      or ep_return_identity_kernel; then ep_signal_kernel raises back flags
-//   6. ep_wait_kernel (sender) waits for all back flags; unpermute reads the
-//      local back buffer
-// Replicated ("hot") experts: every rank holds its own copy of the experts in
+//      or ep_return_identity_kernel; the last CTA of either raises back
+//      flag = e on every peer
+//   5. unpermute (unpermute.cu): its copy warps wait for all back flags, then
+//      combine the local back buffer
+// // Replicated ("hot") experts: every rank holds its own copy of the experts in
 // a set H (the same on all ranks, moe_b200_ep_set_replicated); a row routed
 // to an expert of H never leaves its rank: the dispatch stores it into a local
 // block after the senders' blocks of the own receive buffer, and the expert
@@ -52,18 +53,19 @@ namespace moe_b200 {
 int fail(int code, const char* fmt, ...);
 int cuda_fail(cudaError_t err, const char* where);
 cudaError_t launch_route_scan(const int32_t* asgn, int T, int K, int E, int32_t* expert_count,
-                              int32_t* expert_start, void* ws, cudaStream_t stream);
+                              int32_t* expert_start, void* ws, cudaStream_t stream, const EpPublish* pub);
 cudaError_t launch_unpermute(const void* y, const float* packed_w, const int32_t* slot_pos, int T, int K,
-                             int d, int dtype, void* out, cudaStream_t stream);
+                             int d, int dtype, void* out, cudaStream_t stream, const EpWait* wait);
 int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* seg_expert, int nseg, int rows,
                         int d, int I, int E, const void* w_gate_up, const void* w_down, int dtype, void* h,
                         void* y, cudaStream_t s, char* const* dst_base, const int32_t* seg_src,
                         const int32_t* seg_dst_row, int seg_groups, int seg_group_len, const int32_t* gather_rows,
-                        int gather_T);
+                        int gather_T, const EpSignal* sig);
 
 constexpr int kEpMaxRanks = 64;
 
 constexpr int kEpMaxExperts = 1024;
+constexpr int kInboxSmemMax = 4096;  // counts copied to shared memory up to N*E of this (16 KB)
 
 struct EpGeom {
     int nranks, rank, E, K, d, max_tokens;
@@ -71,7 +73,7 @@ struct EpGeom {
     uint32_t hot[kEpMaxExperts / 32];  // replicated experts (bit e)
     int nhot;                          // |H|
     int lrange;                        // experts of this rank's range that are not replicated
-    size_t off_cflag, off_dflag, off_bflag, off_inbox, off_recv, off_back, total;
+    size_t off_cflag, off_dflag, off_bflag, off_count, off_inbox, off_recv, off_back, total;
     int64_t recv_cap;
     uint64_t timeout_ns;
 };
@@ -85,7 +87,14 @@ struct EpContext {
     char** peer_dev = nullptr;   // device array: every rank's region in this address space
     char** back_dev = nullptr;   // device array: every rank's back buffer
     bool connected = false;
+    uint64_t epoch = 0;          // largest epoch enqueued so far
+    int32_t* seg = nullptr;      // moe_b200_ep_step's segment table: 4 arrays of kEpMaxSegs
 };
+
+// Segments of one rank's receive buffer: nranks * (its range experts) +
+// replicated experts <= 64 * 1024 + 1024 in the worst case; the table of
+// moe_b200_ep_step holds the common case and the entry point checks.
+constexpr int kEpMaxSegs = 4096;
 
 static size_t al4k(size_t x) { return (x + 4095) & ~size_t(4095); }
 
@@ -93,15 +102,6 @@ static size_t al4k(size_t x) { return (x + 4095) & ~size_t(4095); }
 
 __host__ __device__ __forceinline__ bool ep_is_hot(const EpGeom& g, int e) {
     return (g.hot[e >> 5] >> (e & 31)) & 1u;
-}
-
-__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
-    uint64_t v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 // Bounded wait until flags[i] >= epoch for i in [0, n), one thread per flag.
@@ -123,19 +123,6 @@ __device__ bool wait_flags(const uint64_t* flags, int n, uint64_t epoch, uint64_
     return *s_fail == 0;
 }
 
-__global__ void __launch_bounds__(256)
-ep_publish_kernel(EpGeom g, char* const* __restrict__ peer, const int32_t* __restrict__ expert_count,
-                  uint64_t epoch) {
-    for (int p = 0; p < g.nranks; ++p) {
-        int32_t* dst = reinterpret_cast<int32_t*>(peer[p] + g.off_inbox) + size_t(g.rank) * g.E;
-        for (int e = threadIdx.x; e < g.E; e += blockDim.x) dst[e] = expert_count[e];
-    }
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x < g.nranks)
-        st_release_sys(reinterpret_cast<uint64_t*>(peer[threadIdx.x] + g.off_cflag) + g.rank, epoch);
-}
-
 // Warp per token: row read once (16-byte loads), stored to the receive buffer
 // of the rank owning each slot's expert.
 __global__ void __launch_bounds__(256)
@@ -145,12 +132,13 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
                         float* __restrict__ packed_w, int32_t* __restrict__ perm,
                         int32_t* __restrict__ slot_pos, WsHeader* __restrict__ hdr,
                         uint64_t* __restrict__ status, size_t status_words, uint64_t epoch,
-                        uint32_t* __restrict__ dev_status) {
+                        uint32_t* __restrict__ dev_status, int inbox_smem) {
     __shared__ int s_fail;
     // per expert e: the rank whose receive buffer takes its rows, and the
     // receive row of packed position p there = s_dst[e] + p
     extern __shared__ int64_t s_dst[];                          // [E]
     int32_t* s_owner = reinterpret_cast<int32_t*>(s_dst + g.E);  // [E]
+    int32_t* s_inbox = s_owner + g.E;                            // [N][E] when inbox_smem
     const int K = g.K, nvec = g.d / 8;
     if (threadIdx.x == 0) s_fail = 0;
     __syncthreads();
@@ -160,6 +148,13 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
     wait_flags(reinterpret_cast<const uint64_t*>(mine + g.off_cflag), g.nranks, epoch, g.timeout_ns, dev_status,
                &s_fail);
     const int32_t* inbox = reinterpret_cast<const int32_t*>(mine + g.off_inbox);
+    if (inbox_smem) {
+        // one coalesced pass over every rank's counts, so the serial prefix
+        // loops below read shared memory instead of chains of global loads
+        for (int i = threadIdx.x; i < g.nranks * g.E; i += blockDim.x) s_inbox[i] = inbox[i];
+        __syncthreads();
+        inbox = s_inbox;
+    }
     const int32_t* own = inbox + size_t(g.rank) * g.E;  // this rank's counts
     if (threadIdx.x < g.nranks) {
         // receiver r: this sender's block follows the blocks of senders < rank;
@@ -230,18 +225,12 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
             }
         }
     }
-    // The last CTA to finish announces the rows to every receiver.
+    // The last CTA to finish announces the rows to every receiver (unless a
+    // CTA gave up waiting for the counts: then the receivers time out too).
     __threadfence_system();
     __syncthreads();
-    if (threadIdx.x == 0) {
-        const uint32_t prev = atomicAdd(&hdr->pad[0], 1u);
-        if (prev == gridDim.x - 1) {
-            hdr->pad[0] = 0;
-            __threadfence_system();
-            for (int p = 0; p < g.nranks; ++p)
-                st_release_sys(reinterpret_cast<uint64_t*>(peer[p] + g.off_dflag) + g.rank, epoch);
-        }
-    }
+    if (threadIdx.x == 0)
+        ep_signal_done(EpSignal{peer, g.off_dflag, hdr->pad, g.rank, g.nranks, epoch}, s_fail != 0);
 }
 
 // Receiver: wait for every sender's rows, then the segment table of the
@@ -249,7 +238,8 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
 __global__ void __launch_bounds__(256)
 ep_receive_kernel(EpGeom g, char* const* __restrict__ peer, uint64_t epoch, int32_t* __restrict__ seg_start,
                   int32_t* __restrict__ seg_expert, int32_t* __restrict__ seg_src,
-                  int32_t* __restrict__ seg_dst_row, uint32_t* __restrict__ dev_status) {
+                  int32_t* __restrict__ seg_dst_row, uint32_t* __restrict__ dev_status, int inbox_smem) {
+    extern __shared__ int32_t s_inbox[];  // [N][E] when inbox_smem
     __shared__ int s_fail;
     __shared__ int32_t warp_tot[8];
     __shared__ int32_t carry;
@@ -262,6 +252,10 @@ ep_receive_kernel(EpGeom g, char* const* __restrict__ peer, uint64_t epoch, int3
     wait_flags(reinterpret_cast<const uint64_t*>(mine + g.off_dflag), g.nranks, epoch, g.timeout_ns, dev_status,
                &s_fail);
     const int32_t* inbox = reinterpret_cast<const int32_t*>(mine + g.off_inbox);
+    if (inbox_smem) {
+        for (int i = threadIdx.x; i < g.nranks * g.E; i += blockDim.x) s_inbox[i] = inbox[i];
+        inbox = s_inbox;   // published by the __syncthreads below
+    }
     // local experts: [non-replicated experts of the range] + [replicated]
     __shared__ int16_t s_local[kEpMaxExperts];
     if (threadIdx.x == 0) {
@@ -317,7 +311,7 @@ ep_receive_kernel(EpGeom g, char* const* __restrict__ peer, uint64_t epoch, int3
 __global__ void __launch_bounds__(256)
 ep_return_identity_kernel(EpGeom g, char* const* __restrict__ back, const uint4* __restrict__ recv,
                           const int32_t* __restrict__ seg_start, const int32_t* __restrict__ seg_src,
-                          const int32_t* __restrict__ seg_dst_row, int nseg) {
+                          const int32_t* __restrict__ seg_dst_row, int nseg, EpSignal sig) {
     pdl_wait_primary();
     __shared__ int64_t s_lo[kEpMaxRanks + 2];
     __shared__ int64_t s_max;
@@ -353,26 +347,10 @@ ep_return_identity_kernel(EpGeom g, char* const* __restrict__ back, const uint4*
         const uint4* src = recv + row * nvec;
         for (int i = lane; i < nvec; i += 32) st_v4(dst + i, ld_nc_v4(src + i));
     }
+    // the last CTA to finish raises the back flags of every sender
     __threadfence_system();
-}
-
-// Raise flag word `flag_off`[rank] = epoch on every rank (after all prior
-// work of this stream, whose peer stores were fenced system-wide).
-__global__ void ep_signal_kernel(EpGeom g, char* const* __restrict__ peer, size_t flag_off, uint64_t epoch) {
-    pdl_wait_primary();
-    __threadfence_system();
-    if (threadIdx.x < g.nranks)
-        st_release_sys(reinterpret_cast<uint64_t*>(peer[threadIdx.x] + flag_off) + g.rank, epoch);
-}
-
-__global__ void ep_wait_kernel(EpGeom g, const char* __restrict__ mine, size_t flag_off, uint64_t epoch,
-                               uint32_t* __restrict__ dev_status) {
-    __shared__ int s_fail;
-    if (threadIdx.x == 0) s_fail = 0;
     __syncthreads();
-    wait_flags(reinterpret_cast<const uint64_t*>(mine + flag_off), g.nranks, epoch, g.timeout_ns, dev_status,
-               &s_fail);
-    __threadfence_system();
+    if (threadIdx.x == 0) ep_signal_done(sig, false);
 }
 
 // ------------------------------------------------------------------ host ----
@@ -427,6 +405,7 @@ int moe_b200_ep_create(int nranks, int rank, int E, int K, int d, int max_tokens
     g.off_cflag = 0;
     g.off_dflag = 8 * kEpMaxRanks;
     g.off_bflag = 16 * kEpMaxRanks;
+    g.off_count = 24 * kEpMaxRanks;  // [0,2): return CTAs done / failed, [2,4): down-GEMM CTAs done / failed
     g.off_inbox = 4096;
     g.off_recv = g.off_inbox + al4k(size_t(nranks) * E * 4);
     g.recv_cap = int64_t(nranks) * max_tokens * K;
@@ -437,8 +416,10 @@ int moe_b200_ep_create(int nranks, int rank, int E, int K, int d, int max_tokens
     if (err == cudaSuccess) err = cudaMalloc(&ctx->region, g.total);
     if (err == cudaSuccess) err = cudaMemset(ctx->region, 0, g.total);
     if (err == cudaSuccess) err = cudaMalloc(&ctx->peer_dev, sizeof(char*) * kEpMaxRanks * 2);
+    if (err == cudaSuccess) err = cudaMalloc(&ctx->seg, sizeof(int32_t) * 4 * (kEpMaxSegs + 1));
     if (err != cudaSuccess) {
         if (ctx->region) cudaFree(ctx->region);
+        if (ctx->peer_dev) cudaFree(ctx->peer_dev);
         delete ctx;
         return cuda_fail(err, "ep_create");
     }
@@ -494,6 +475,7 @@ int moe_b200_ep_destroy(void* c) {
     for (int p = 0; p < ctx->g.nranks; ++p)
         if (ctx->opened[p]) cudaIpcCloseMemHandle(ctx->peer_host[p]);
     if (ctx->peer_dev) cudaFree(ctx->peer_dev);
+    if (ctx->seg) cudaFree(ctx->seg);
     if (ctx->region) cudaFree(ctx->region);
     delete ctx;
     return MOE_B200_OK;
@@ -551,11 +533,11 @@ int64_t moe_b200_ep_recv_capacity(void* c) {
     return ctx ? ctx->g.recv_cap : 0;
 }
 
-int moe_b200_ep_dispatch(void* c, uint64_t epoch, const void* emb, const int32_t* asgn, const float* wts, int T,
-                         float* packed_weights, int32_t* perm, int32_t* expert_count, int32_t* expert_start,
-                         int32_t* slot_pos, void* workspace, size_t workspace_bytes, void* stream) {
-    EpContext* ctx = as_ctx(c);
-    if (!ctx || !ctx->connected) return fail(MOE_B200_ERR_INVALID_ARG, "ep_dispatch: context not connected");
+// Enqueue helpers shared by the stage entry points and moe_b200_ep_step.
+static int ep_enqueue_dispatch(EpContext* ctx, uint64_t epoch, const void* emb, const int32_t* asgn,
+                               const float* wts, int T, float* packed_weights, int32_t* perm,
+                               int32_t* expert_count, int32_t* expert_start, int32_t* slot_pos, void* workspace,
+                               size_t workspace_bytes, cudaStream_t s) {
     const EpGeom& g = ctx->g;
     if (T < 1 || T > g.max_tokens || !emb || !asgn || !perm || !expert_count || !expert_start || !slot_pos ||
         (packed_weights && !wts))
@@ -568,18 +550,18 @@ int moe_b200_ep_dispatch(void* c, uint64_t epoch, const void* emb, const int32_t
                     plan.total_bytes);
     uint32_t* st = device_status_word();
     if (!st) return fail(MOE_B200_ERR_CUDA, "ep_dispatch: device status word unavailable");
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t err = launch_route_scan(asgn, T, g.K, g.E, expert_count, expert_start, workspace, s);
-    if (err == cudaSuccess) {
-        ep_publish_kernel<<<1, 256, 0, s>>>(g, ctx->peer_dev, expert_count, epoch);
-        err = cudaGetLastError();
-    }
+    // the scan's last tile publishes the counts to every rank
+    const EpPublish pub{ctx->peer_dev, g.off_inbox, g.off_cflag, g.rank, g.nranks, epoch};
+    cudaError_t err = launch_route_scan(asgn, T, g.K, g.E, expert_count, expert_start, workspace, s, &pub);
     if (err == cudaSuccess) {
         char* base = static_cast<char*>(workspace);
         int grid = sm_count_ep() * 4;
         const int want = (T + 7) / 8;
         if (grid > want) grid = want;
-        cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(256), size_t(g.E) * 12, s);
+        // the counts inbox goes to shared memory when it is small (N*E <= 4096)
+        const int inbox_smem = int64_t(g.nranks) * g.E <= kInboxSmemMax ? 1 : 0;
+        const size_t smem = size_t(g.E) * 12 + (inbox_smem ? size_t(g.nranks) * g.E * 4 : 0);
+        cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(256), smem, s);
         cudaLaunchAttribute attr = pdl_attr();
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
@@ -589,81 +571,162 @@ int moe_b200_ep_dispatch(void* c, uint64_t epoch, const void* emb, const int32_t
                                  static_cast<const int32_t*>(expert_start), T, packed_weights, perm, slot_pos,
                                  reinterpret_cast<WsHeader*>(base),
                                  reinterpret_cast<uint64_t*>(base + plan.status_off),
-                                 size_t(plan.num_tiles) * size_t(g.E), epoch, st);
+                                 size_t(plan.num_tiles) * size_t(g.E), epoch, st, inbox_smem);
     }
+    if (err == cudaSuccess && epoch > ctx->epoch) ctx->epoch = epoch;
     return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "ep_dispatch launch");
 }
 
-int moe_b200_ep_receive(void* c, uint64_t epoch, int32_t* seg_start, int32_t* seg_expert, int32_t* seg_src,
-                        int32_t* seg_dst_row, void* stream) {
-    EpContext* ctx = as_ctx(c);
-    if (!ctx || !ctx->connected) return fail(MOE_B200_ERR_INVALID_ARG, "ep_receive: context not connected");
+static int ep_enqueue_receive(EpContext* ctx, uint64_t epoch, int32_t* seg_start, int32_t* seg_expert,
+                              int32_t* seg_src, int32_t* seg_dst_row, cudaStream_t s) {
     if (!seg_start || !seg_expert || !seg_src || !seg_dst_row)
         return fail(MOE_B200_ERR_INVALID_ARG, "ep_receive: null segment buffer");
     uint32_t* st = device_status_word();
     if (!st) return fail(MOE_B200_ERR_CUDA, "ep_receive: device status word unavailable");
-    ep_receive_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        ctx->g, ctx->peer_dev, epoch, seg_start, seg_expert, seg_src, seg_dst_row, st);
+    const int inbox_smem = int64_t(ctx->g.nranks) * ctx->g.E <= kInboxSmemMax ? 1 : 0;
+    const size_t smem = inbox_smem ? size_t(ctx->g.nranks) * ctx->g.E * 4 : 0;
+    ep_receive_kernel<<<1, 256, smem, s>>>(ctx->g, ctx->peer_dev, epoch, seg_start, seg_expert, seg_src,
+                                           seg_dst_row, st, inbox_smem);
     cudaError_t err = cudaGetLastError();
     return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "ep_receive launch");
 }
 
-int moe_b200_ep_return_identity(void* c, uint64_t epoch, const int32_t* seg_start, const int32_t* seg_src,
-                                const int32_t* seg_dst_row, void* stream) {
-    EpContext* ctx = as_ctx(c);
-    if (!ctx || !ctx->connected) return fail(MOE_B200_ERR_INVALID_ARG, "ep_return_identity: not connected");
+static EpSignal back_signal(EpContext* ctx, int which, uint64_t epoch) {
+    const EpGeom& g = ctx->g;
+    return EpSignal{ctx->peer_dev, g.off_bflag,
+                    reinterpret_cast<uint32_t*>(ctx->region + g.off_count) + 2 * which, g.rank, g.nranks, epoch};
+}
+
+static int ep_enqueue_return_identity(EpContext* ctx, uint64_t epoch, const int32_t* seg_start,
+                                      const int32_t* seg_src, const int32_t* seg_dst_row, cudaStream_t s) {
     const EpGeom& g = ctx->g;
     const int nseg = g.nranks * g.lrange + g.nhot;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaLaunchConfig_t cfg = pdl_config(dim3(sm_count_ep() * 4), dim3(256), 0, s);
     cudaLaunchAttribute attr = pdl_attr();
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     cudaError_t err = cudaLaunchKernelEx(&cfg, ep_return_identity_kernel, g, static_cast<char* const*>(ctx->back_dev),
                                          reinterpret_cast<const uint4*>(ctx->region + g.off_recv), seg_start, seg_src,
-                                         seg_dst_row, nseg);
-    if (err == cudaSuccess) {
-        ep_signal_kernel<<<1, 64, 0, s>>>(g, ctx->peer_dev, g.off_bflag, epoch);
-        err = cudaGetLastError();
-    }
+                                         seg_dst_row, nseg, back_signal(ctx, 0, epoch));
     return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "ep_return_identity launch");
+}
+
+static int ep_enqueue_ffn_return(EpContext* ctx, uint64_t epoch, const int32_t* seg_start,
+                                 const int32_t* seg_expert, const int32_t* seg_src, const int32_t* seg_dst_row,
+                                 int I, const void* w_gate_up, const void* w_down, int dtype, void* h,
+                                 cudaStream_t s) {
+    const EpGeom& g = ctx->g;
+    // GEMM 2's epilogue stores each finished tile straight into the back
+    // buffer of the rank that sent its rows (scatter mode); its last CTA
+    // raises the back flags.  Local experts: the range's non-replicated ones,
+    // then the replicated ones.
+    const EpSignal sig = back_signal(ctx, 1, epoch);
+    return grouped_swiglu_impl(ctx->region + g.off_recv, seg_start, seg_expert, g.nranks * g.lrange + g.nhot,
+                               int(g.recv_cap), g.d, I, g.lrange + g.nhot, w_gate_up, w_down, dtype, h,
+                               ctx->region + g.off_recv, s, ctx->back_dev, seg_src, seg_dst_row, g.nranks, g.lrange,
+                               nullptr, 0, &sig);
+}
+
+static int ep_enqueue_combine(EpContext* ctx, uint64_t epoch, const float* packed_weights, const int32_t* slot_pos,
+                              int T, int dtype, void* out, cudaStream_t s) {
+    const EpGeom& g = ctx->g;
+    if (T < 1 || T > g.max_tokens || !packed_weights || !slot_pos || !out)
+        return fail(MOE_B200_ERR_INVALID_ARG, "ep_combine: need 1 <= T <= max_tokens and all buffers");
+    if (dtype != MOE_B200_F16 && dtype != MOE_B200_BF16)
+        return fail(MOE_B200_ERR_INVALID_ARG, "ep_combine: dtype %d is neither F16 nor BF16", dtype);
+    // the unpermute's copy warps wait for every rank's back flag
+    const EpWait wt{reinterpret_cast<const uint64_t*>(ctx->region + g.off_bflag), g.nranks, epoch, g.timeout_ns};
+    cudaError_t err = launch_unpermute(ctx->region + g.off_back, packed_weights, slot_pos, T, g.K, g.d, dtype, out, s,
+                                       &wt);
+    return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "ep_combine launch");
+}
+
+static EpContext* connected_ctx(void* c, const char* what) {
+    EpContext* ctx = as_ctx(c);
+    if (!ctx || !ctx->connected) {
+        fail(MOE_B200_ERR_INVALID_ARG, "%s: context not connected", what);
+        return nullptr;
+    }
+    return ctx;
+}
+
+int moe_b200_ep_dispatch(void* c, uint64_t epoch, const void* emb, const int32_t* asgn, const float* wts, int T,
+                         float* packed_weights, int32_t* perm, int32_t* expert_count, int32_t* expert_start,
+                         int32_t* slot_pos, void* workspace, size_t workspace_bytes, void* stream) {
+    EpContext* ctx = connected_ctx(c, "ep_dispatch");
+    if (!ctx) return MOE_B200_ERR_INVALID_ARG;
+    return ep_enqueue_dispatch(ctx, epoch, emb, asgn, wts, T, packed_weights, perm, expert_count, expert_start,
+                               slot_pos, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int moe_b200_ep_receive(void* c, uint64_t epoch, int32_t* seg_start, int32_t* seg_expert, int32_t* seg_src,
+                        int32_t* seg_dst_row, void* stream) {
+    EpContext* ctx = connected_ctx(c, "ep_receive");
+    if (!ctx) return MOE_B200_ERR_INVALID_ARG;
+    return ep_enqueue_receive(ctx, epoch, seg_start, seg_expert, seg_src, seg_dst_row,
+                              static_cast<cudaStream_t>(stream));
+}
+
+int moe_b200_ep_return_identity(void* c, uint64_t epoch, const int32_t* seg_start, const int32_t* seg_src,
+                                const int32_t* seg_dst_row, void* stream) {
+    EpContext* ctx = connected_ctx(c, "ep_return_identity");
+    if (!ctx) return MOE_B200_ERR_INVALID_ARG;
+    if (!seg_start || !seg_src || !seg_dst_row)
+        return fail(MOE_B200_ERR_INVALID_ARG, "ep_return_identity: null segment buffer");
+    return ep_enqueue_return_identity(ctx, epoch, seg_start, seg_src, seg_dst_row, static_cast<cudaStream_t>(stream));
 }
 
 int moe_b200_ep_ffn_return(void* c, uint64_t epoch, const int32_t* seg_start, const int32_t* seg_expert,
                            const int32_t* seg_src, const int32_t* seg_dst_row, int I, const void* w_gate_up,
                            const void* w_down, int dtype, void* h, void* stream) {
-    EpContext* ctx = as_ctx(c);
-    if (!ctx || !ctx->connected) return fail(MOE_B200_ERR_INVALID_ARG, "ep_ffn_return: not connected");
-    const EpGeom& g = ctx->g;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // GEMM 2's epilogue stores each finished tile straight into the back
-    // buffer of the rank that sent its rows (scatter mode).  Local experts:
-    // the range's non-replicated ones, then the replicated ones.
-    int st = grouped_swiglu_impl(ctx->region + g.off_recv, seg_start, seg_expert, g.nranks * g.lrange + g.nhot,
-                                 int(g.recv_cap), g.d, I, g.lrange + g.nhot, w_gate_up, w_down, dtype, h,
-                                 ctx->region + g.off_recv, s, ctx->back_dev, seg_src, seg_dst_row, g.nranks,
-                                 g.lrange, nullptr, 0);
-    if (st != MOE_B200_OK) return st;
-    ep_signal_kernel<<<1, 64, 0, s>>>(g, ctx->peer_dev, g.off_bflag, epoch);
-    cudaError_t err = cudaGetLastError();
-    return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "ep_ffn_return signal");
+    EpContext* ctx = connected_ctx(c, "ep_ffn_return");
+    if (!ctx) return MOE_B200_ERR_INVALID_ARG;
+    return ep_enqueue_ffn_return(ctx, epoch, seg_start, seg_expert, seg_src, seg_dst_row, I, w_gate_up, w_down, dtype,
+                                 h, static_cast<cudaStream_t>(stream));
 }
 
 int moe_b200_ep_combine(void* c, uint64_t epoch, const float* packed_weights, const int32_t* slot_pos, int T,
                         int dtype, void* out, void* stream) {
-    EpContext* ctx = as_ctx(c);
-    if (!ctx || !ctx->connected) return fail(MOE_B200_ERR_INVALID_ARG, "ep_combine: not connected");
+    EpContext* ctx = connected_ctx(c, "ep_combine");
+    if (!ctx) return MOE_B200_ERR_INVALID_ARG;
+    return ep_enqueue_combine(ctx, epoch, packed_weights, slot_pos, T, dtype, out, static_cast<cudaStream_t>(stream));
+}
+
+int moe_b200_ep_step(void* c, const void* emb, const int32_t* asgn, const float* wts, int T, int I,
+                     const void* w_gate_up, const void* w_down, int dtype, void* h, float* packed_weights,
+                     int32_t* perm, int32_t* expert_count, int32_t* expert_start, int32_t* slot_pos,
+                     void* workspace, size_t workspace_bytes, void* out, void* stream) {
+    EpContext* ctx = connected_ctx(c, "ep_step");
+    if (!ctx) return MOE_B200_ERR_INVALID_ARG;
     const EpGeom& g = ctx->g;
-    if (T < 1 || T > g.max_tokens || !packed_weights || !slot_pos || !out)
-        return fail(MOE_B200_ERR_INVALID_ARG, "ep_combine: need 1 <= T <= max_tokens and all buffers");
-    uint32_t* st = device_status_word();
-    if (!st) return fail(MOE_B200_ERR_CUDA, "ep_combine: device status word unavailable");
+    const int nseg = g.nranks * g.lrange + g.nhot;
+    if (nseg > kEpMaxSegs)
+        return fail(MOE_B200_ERR_UNSUPPORTED, "ep_step: %d receive segments exceed %d; use the stage entry points",
+                    nseg, kEpMaxSegs);
+    if (!packed_weights) return fail(MOE_B200_ERR_INVALID_ARG, "ep_step: packed_weights is required");
+    const bool identity = w_gate_up == nullptr && w_down == nullptr;
+    if (!identity && (!w_gate_up || !w_down || !h || I < 1))
+        return fail(MOE_B200_ERR_INVALID_ARG, "ep_step: the FFN needs w_gate_up, w_down, h and I >= 1");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    ep_wait_kernel<<<1, 64, 0, s>>>(g, ctx->region, g.off_bflag, epoch, st);
-    cudaError_t err = cudaGetLastError();
-    if (err == cudaSuccess)
-        err = launch_unpermute(ctx->region + g.off_back, packed_weights, slot_pos, T, g.K, g.d, dtype, out, s);
-    return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "ep_combine launch");
+    const uint64_t epoch = ctx->epoch + 1;
+    int32_t* seg_start = ctx->seg;
+    int32_t* seg_expert = seg_start + (kEpMaxSegs + 1);
+    int32_t* seg_src = seg_expert + (kEpMaxSegs + 1);
+    int32_t* seg_dst_row = seg_src + (kEpMaxSegs + 1);
+    int st = ep_enqueue_dispatch(ctx, epoch, emb, asgn, wts, T, packed_weights, perm, expert_count, expert_start,
+                                 slot_pos, workspace, workspace_bytes, s);
+    if (st == MOE_B200_OK) st = ep_enqueue_receive(ctx, epoch, seg_start, seg_expert, seg_src, seg_dst_row, s);
+    if (st == MOE_B200_OK)
+        st = identity ? ep_enqueue_return_identity(ctx, epoch, seg_start, seg_src, seg_dst_row, s)
+                      : ep_enqueue_ffn_return(ctx, epoch, seg_start, seg_expert, seg_src, seg_dst_row, I, w_gate_up,
+                                              w_down, dtype, h, s);
+    if (st == MOE_B200_OK) st = ep_enqueue_combine(ctx, epoch, packed_weights, slot_pos, T, dtype, out, s);
+    return st;
+}
+
+uint64_t moe_b200_ep_epoch(void* c) {
+    EpContext* ctx = as_ctx(c);
+    return ctx ? ctx->epoch : 0;
 }
 
 }  // extern "C"

@@ -205,7 +205,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                     uint32_t* __restrict__ dev_status, char* const* __restrict__ dst_base,
                     const int32_t* __restrict__ seg_src, const int32_t* __restrict__ seg_dst_row,
                     int seg_groups, int seg_group_len, const int32_t* __restrict__ gather_rows,
-                    int gather_limit) {
+                    int gather_limit, EpSignal sig) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte aligned stage buffers (SW128 atoms), control block after them.
     unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -534,6 +534,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     if (dst_base && warp >= 2) __threadfence_system();
     tc_fence_before();
     __syncthreads();
+    // expert parallel: the last CTA to finish raises the senders' back flags
+    if (sig.peer && threadIdx.x == 0) ep_signal_done(sig, *abort_flag != 0);
     if (CG == 2) cluster_sync();  // no CTA leaves while its pair may still signal it
     tc_fence_after();
     if (warp == 1) {
@@ -580,7 +582,8 @@ static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb_, co
                                uint32_t* st, cudaStream_t stream, char* const* dst_base = nullptr,
                                const int32_t* seg_src = nullptr, const int32_t* seg_dst_row = nullptr,
                                int seg_groups = 1, int seg_group_len = 0, const int32_t* gather_rows = nullptr,
-                               int gather_limit = 0) {
+                               int gather_limit = 0, const EpSignal* sig = nullptr) {
+    EpSignal no_sig{};
     const size_t smem = ffn_smem_bytes<CG>(nseg);
     auto kern = grouped_gemm_kernel<EPI, DT, CG>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -607,7 +610,8 @@ static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb_, co
     cfg.gridDim = dim3(CG * groups);
     return cudaLaunchKernelEx(&cfg, kern, ma, mb_, seg_start, seg_expert, nseg, kdim, b_rows_per_expert, n_out,
                               n_blocks, split, static_cast<uint16_t*>(out), out_stride, st, dst_base, seg_src,
-                              seg_dst_row, seg_groups, seg_group_len, gather_rows, gather_limit);
+                              seg_dst_row, seg_groups, seg_group_len, gather_rows, gather_limit,
+                              sig ? *sig : no_sig);
 }
 
 template <int DT>
@@ -615,7 +619,8 @@ static cudaError_t launch_ffn(int cg, const CUtensorMap& mx, const CUtensorMap& 
                               const CUtensorMap& mwd, const int32_t* seg_start, const int32_t* seg_expert, int nseg,
                               int rows, int d, int I, void* h, void* y, uint32_t* st, cudaStream_t s,
                               char* const* dst_base, const int32_t* seg_src, const int32_t* seg_dst_row,
-                              int seg_groups, int seg_group_len, const int32_t* gather_rows, int gather_T) {
+                              int seg_groups, int seg_group_len, const int32_t* gather_rows, int gather_T,
+                              const EpSignal* sig) {
     const int nb1 = (I + kTileN / 2 - 1) / (kTileN / 2);
     const int nb2 = (d + kTileN - 1) / kTileN;
     // The gathered form of GEMM 1 runs on single SMs.
@@ -628,9 +633,11 @@ static cudaError_t launch_ffn(int cg, const CUtensorMap& mx, const CUtensorMap& 
                                              gather_T);
     if (err != cudaSuccess) return err;
     return (cg & 2) ? launch_gemm<kEpiStore, DT, 2>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0, y, d,
-                                                    st, s, dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len)
+                                                    st, s, dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len,
+                                                    nullptr, 0, sig)
                     : launch_gemm<kEpiStore, DT, 1>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0, y, d,
-                                                    st, s, dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len);
+                                                    st, s, dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len,
+                                                    nullptr, 0, sig);
 }
 
 int fail(int code, const char* fmt, ...);
@@ -643,7 +650,7 @@ int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* 
                         int d, int I, int E, const void* w_gate_up, const void* w_down, int dtype, void* h,
                         void* y, cudaStream_t s, char* const* dst_base, const int32_t* seg_src,
                         const int32_t* seg_dst_row, int seg_groups, int seg_group_len, const int32_t* gather_rows,
-                        int gather_T) {
+                        int gather_T, const EpSignal* sig) {
     if (nseg < 1 || rows < 0 || d < 1 || I < 1 || E < 1)
         return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: need nseg>=1, rows>=0, d>=1, I>=1, E>=1");
     if (nseg > kMaxSegments)
@@ -660,7 +667,7 @@ int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* 
     if (dst_base && (!seg_src || !seg_dst_row))
         return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: scatter mode needs seg_src and seg_dst_row");
     if (al % 16 != 0) return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: pointers must be 16-byte aligned");
-    if (rows == 0) return MOE_B200_OK;
+    if (rows == 0 && !sig) return MOE_B200_OK;
     uint32_t* st = device_status_word();
     if (!st) return fail(MOE_B200_ERR_CUDA, "grouped_swiglu: device status word unavailable");
     const int cg = ffn_cta_groups(rows, nseg);
@@ -679,20 +686,132 @@ int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* 
         dtype == MOE_B200_BF16
             ? launch_ffn<MOE_B200_BF16>(cg, mx, mwgu, mh, mwd, seg_start, seg_expert, nseg, rows, d, I, h, y, st, s,
                                         dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len, gather_rows,
-                                        gather_T)
+                                        gather_T, sig)
             : launch_ffn<MOE_B200_F16>(cg, mx, mwgu, mh, mwd, seg_start, seg_expert, nseg, rows, d, I, h, y, st, s,
                                        dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len, gather_rows,
-                                       gather_T);
+                                       gather_T, sig);
     return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "grouped_swiglu launch");
 }
 }  // namespace moe_b200
+
+namespace moe_b200 {
+// Activation-free grouped FFN (the reference's expert: up-projection, then
+// down-projection, each result rounded once to 16 bits), on the same
+// persistent tcgen05 kernel in its plain-store form:
+//   mid[r] = x[r] . Wup[e]^T   (K = d, N = F)      y[r] = mid[r] . Wdown[e]^T   (K = F, N = d)
+template <int DT>
+static cudaError_t launch_plain_ffn(int cg, const CUtensorMap& mx, const CUtensorMap& mwu, const CUtensorMap& mmid,
+                                    const CUtensorMap& mwd, const int32_t* seg_start, const int32_t* seg_expert,
+                                    int nseg, int rows, int d, int F, void* mid, void* y, uint32_t* st,
+                                    cudaStream_t s) {
+    const int nb1 = (F + kTileN - 1) / kTileN;
+    const int nb2 = (d + kTileN - 1) / kTileN;
+    cudaError_t err = (cg & 1) ? launch_gemm<kEpiStore, DT, 2>(mx, mwu, seg_start, seg_expert, nseg, rows, d, F, F,
+                                                              nb1, 0, mid, F, st, s)
+                               : launch_gemm<kEpiStore, DT, 1>(mx, mwu, seg_start, seg_expert, nseg, rows, d, F, F,
+                                                              nb1, 0, mid, F, st, s);
+    if (err != cudaSuccess) return err;
+    return (cg & 2) ? launch_gemm<kEpiStore, DT, 2>(mmid, mwd, seg_start, seg_expert, nseg, rows, F, d, d, nb2, 0, y,
+                                                    d, st, s)
+                    : launch_gemm<kEpiStore, DT, 1>(mmid, mwd, seg_start, seg_expert, nseg, rows, F, d, d, nb2, 0, y,
+                                                    d, st, s);
+}
+
+int grouped_ffn_plain_impl(const void* x, const int32_t* seg_start, const int32_t* seg_expert, int nseg, int rows,
+                           int d, int F, int E, const void* w_up, const void* w_down, int dtype, void* mid, void* y,
+                           cudaStream_t s) {
+    if (nseg < 1 || rows < 0 || d < 1 || F < 1 || E < 1)
+        return fail(MOE_B200_ERR_INVALID_ARG, "grouped_ffn: need nseg>=1, rows>=0, d>=1, F>=1, E>=1");
+    if (nseg > kMaxSegments)
+        return fail(MOE_B200_ERR_UNSUPPORTED, "grouped_ffn: %d segments exceed %d", nseg, kMaxSegments);
+    if (dtype != MOE_B200_F16 && dtype != MOE_B200_BF16)
+        return fail(MOE_B200_ERR_INVALID_ARG, "grouped_ffn: dtype %d is neither F16 nor BF16", dtype);
+    if (d % 16 != 0 || F % 16 != 0)
+        return fail(MOE_B200_ERR_UNSUPPORTED, "grouped_ffn: d and F must be multiples of 16 (d=%d F=%d)", d, F);
+    if (!x || !seg_start || !w_up || !w_down || !mid || !y)
+        return fail(MOE_B200_ERR_INVALID_ARG, "grouped_ffn: null pointer");
+    const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w_up) |
+                         reinterpret_cast<uintptr_t>(w_down) | reinterpret_cast<uintptr_t>(mid) |
+                         reinterpret_cast<uintptr_t>(y);
+    if (al % 16 != 0) return fail(MOE_B200_ERR_INVALID_ARG, "grouped_ffn: pointers must be 16-byte aligned");
+    if (rows == 0) return MOE_B200_OK;
+    uint32_t* st = device_status_word();
+    if (!st) return fail(MOE_B200_ERR_CUDA, "grouped_ffn: device status word unavailable");
+    const int cg = ffn_cta_groups(rows, nseg);
+    // B boxes: a CTA of an SM pair holds half of the 256 B rows of a tile
+    CUtensorMap mx, mwu, mmid, mwd;
+    if (!make_map(&mx, x, rows, d, kTileM, dtype) ||
+        !make_map(&mwu, w_up, int64_t(E) * F, d, (cg & 1) ? kTileN / 2 : kTileN, dtype) ||
+        !make_map(&mmid, mid, rows, F, kTileM, dtype) ||
+        !make_map(&mwd, w_down, int64_t(E) * d, F, (cg & 2) ? kTileN / 2 : kTileN, dtype))
+        return fail(MOE_B200_ERR_CUDA, "grouped_ffn: cuTensorMapEncodeTiled failed");
+    const cudaError_t err =
+        dtype == MOE_B200_BF16
+            ? launch_plain_ffn<MOE_B200_BF16>(cg, mx, mwu, mmid, mwd, seg_start, seg_expert, nseg, rows, d, F, mid, y,
+                                              st, s)
+            : launch_plain_ffn<MOE_B200_F16>(cg, mx, mwu, mmid, mwd, seg_start, seg_expert, nseg, rows, d, F, mid, y,
+                                             st, s);
+    return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "grouped_ffn launch");
+}
+
+// Per-expert transpose [E][R][C] -> [E][C][R] of 16-bit words through a
+// 32 x 32 shared-memory tile (coalesced reads and writes): turns the
+// reference's expert weights (W1 [E][d][F], W2 [E][F][d], row-major "B"
+// operands of C = A . B) into the K-major w_up [E][F][d] / w_down [E][d][F].
+__global__ void __launch_bounds__(256)
+transpose_experts_kernel(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, int R, int C) {
+    __shared__ uint16_t tile[32][33];
+    const int e = blockIdx.z;
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    const uint16_t* s = src + size_t(e) * R * C;
+    uint16_t* o = dst + size_t(e) * R * C;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+    for (int j = ty; j < 32; j += 8) {
+        const int r = r0 + j, c = c0 + tx;
+        if (r < R && c < C) tile[j][tx] = s[size_t(r) * C + c];
+    }
+    __syncthreads();
+    for (int j = ty; j < 32; j += 8) {
+        const int c = c0 + j, r = r0 + tx;
+        if (c < C && r < R) o[size_t(c) * R + r] = tile[tx][j];
+    }
+}
+
+static cudaError_t launch_transpose_experts(const void* src, void* dst, int E, int R, int C, cudaStream_t s) {
+    if (E < 1 || R < 1 || C < 1) return cudaSuccess;
+    if (E > 65535) return cudaErrorInvalidValue;
+    dim3 grid((C + 31) / 32, (R + 31) / 32, E);
+    transpose_experts_kernel<<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), R,
+                                                   C);
+    return cudaGetLastError();
+}
+}  // namespace moe_b200
+
+extern "C" int moe_b200_grouped_ffn(const void* x, const int32_t* seg_start, const int32_t* seg_expert, int nseg,
+                                    int rows, int d, int F, int E, const void* w_up, const void* w_down, int dtype,
+                                    void* mid, void* y, void* stream) {
+    return moe_b200::grouped_ffn_plain_impl(x, seg_start, seg_expert, nseg, rows, d, F, E, w_up, w_down, dtype, mid,
+                                            y, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int moe_b200_ffn_weights_from_reference(const void* w1, const void* w2, int E, int d, int F, void* w_up,
+                                                   void* w_down, void* stream) {
+    using namespace moe_b200;
+    if (!w1 || !w2 || !w_up || !w_down || E < 1 || d < 1 || F < 1)
+        return fail(MOE_B200_ERR_INVALID_ARG, "ffn_weights_from_reference: need all buffers and E, d, F >= 1");
+    if (E > 65535) return fail(MOE_B200_ERR_UNSUPPORTED, "ffn_weights_from_reference: E=%d above 65535", E);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t err = launch_transpose_experts(w1, w_up, E, d, F, s);        // [E][d][F] -> [E][F][d]
+    if (err == cudaSuccess) err = launch_transpose_experts(w2, w_down, E, F, d, s);  // [E][F][d] -> [E][d][F]
+    return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "ffn_weights_from_reference launch");
+}
 
 extern "C" int moe_b200_grouped_swiglu(const void* x, const int32_t* seg_start, const int32_t* seg_expert,
                                        int nseg, int rows, int d, int I, int E, const void* w_gate_up,
                                        const void* w_down, int dtype, void* h, void* y, void* stream) {
     return moe_b200::grouped_swiglu_impl(x, seg_start, seg_expert, nseg, rows, d, I, E, w_gate_up, w_down, dtype,
                                          h, y, static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr, 1, 0,
-                                         nullptr, 0);
+                                         nullptr, 0, nullptr);
 }
 
 extern "C" int moe_b200_grouped_swiglu_gather(const void* x_tokens, int T, const int32_t* row_token,
@@ -703,5 +822,5 @@ extern "C" int moe_b200_grouped_swiglu_gather(const void* x_tokens, int T, const
         return moe_b200::fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu_gather: need row_token and T >= 1");
     return moe_b200::grouped_swiglu_impl(x_tokens, seg_start, seg_expert, nseg, rows, d, I, E, w_gate_up, w_down,
                                          dtype, h, y, static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr,
-                                         1, 0, row_token, T);
+                                         1, 0, row_token, T, nullptr);
 }

@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(kScanThreads)
 route_scan_kernel(const int32_t* __restrict__ asgn, int64_t TK, int E, int num_tiles,
                   WsHeader* __restrict__ hdr, uint64_t* __restrict__ status,
                   int32_t* __restrict__ rank, int32_t* __restrict__ expert_count,
-                  int32_t* __restrict__ expert_start) {
+                  int32_t* __restrict__ expert_start, EpPublish pub) {
     extern __shared__ int32_t smem[];
     int32_t* hist = smem;                        // [kScanWarps][E]
     int32_t* tile_excl = smem + kScanWarps * E;  // [E] exclusive prefix of this tile
@@ -199,8 +199,17 @@ route_scan_kernel(const int32_t* __restrict__ asgn, int64_t TK, int E, int num_t
         expert_count[e0 + i] = cnt;
         expert_start[e0 + i] = run;
         run += cnt;
+        // expert parallel: the counts go straight into every rank's inbox
+        for (int p = 0; pub.peer && p < pub.nranks; ++p)
+            reinterpret_cast<int32_t*>(pub.peer[p] + pub.off_inbox)[size_t(pub.rank) * E + e0 + i] = cnt;
     }
     if (tid == kScanThreads - 1) expert_start[E] = warp_off + incl;
+    if (pub.peer) {
+        __threadfence_system();
+        __syncthreads();
+        if (tid < pub.nranks)
+            st_release_sys(reinterpret_cast<uint64_t*>(pub.peer[tid] + pub.off_flag) + pub.rank, pub.epoch);
+    }
 }
 
 
@@ -467,14 +476,15 @@ static int sm_count() {
 // starts in the outputs); used by launch_pack and by the expert-parallel
 // dispatch.
 cudaError_t launch_route_scan(const int32_t* asgn, int T, int K, int E, int32_t* expert_count,
-                              int32_t* expert_start, void* ws, cudaStream_t stream) {
+                              int32_t* expert_start, void* ws, cudaStream_t stream, const EpPublish* pub) {
     const PackPlan plan = plan_pack(T, K, E);
     char* base = static_cast<char*>(ws);
     size_t smem = size_t(kScanWarps + 2) * E * sizeof(int32_t);
+    EpPublish none{};
     route_scan_kernel<<<plan.num_tiles, kScanThreads, smem, stream>>>(
         asgn, int64_t(T) * K, E, plan.num_tiles, reinterpret_cast<WsHeader*>(base),
         reinterpret_cast<uint64_t*>(base + plan.status_off),
-        reinterpret_cast<int32_t*>(base + plan.rank_off), expert_count, expert_start);
+        reinterpret_cast<int32_t*>(base + plan.rank_off), expert_count, expert_start, pub ? *pub : none);
     return cudaGetLastError();
 }
 
@@ -490,7 +500,7 @@ cudaError_t launch_pack(const void* emb, const int32_t* asgn, const float* wts, 
     const int64_t TK = int64_t(T) * K;
     const size_t words = size_t(plan.num_tiles) * size_t(E);
 
-    cudaError_t err = launch_route_scan(asgn, T, K, E, expert_count, expert_start, ws, stream);
+    cudaError_t err = launch_route_scan(asgn, T, K, E, expert_count, expert_start, ws, stream, nullptr);
     if (err != cudaSuccess) return err;
     if (!packed) {
         cudaLaunchConfig_t cfg = pdl_config(dim3(unsigned(std::min<int64_t>((TK + 255) / 256, int64_t(sm_count()) * 8))),

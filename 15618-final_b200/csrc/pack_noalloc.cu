@@ -10,19 +10,25 @@
 // which every GPU that loads the library holds until the process exits.
 //
 // Set-up: the first call on a device (with that device current) looks up the
-// array's device address with cudaGetSymbolAddress and zero-fills it once
-// (a blocking cudaMemset).  Make that first call before any stream capture.
-// In host code the array's name is only a host-side stand-in, so the kernels
-// always receive the looked-up address.
+// array's device address with cudaGetSymbolAddress and remembers it per
+// device ordinal.  Make that first call before any stream capture.  In host
+// code the array's name is only a host-side stand-in, so the kernels always
+// receive the looked-up address.  The remembered address belongs to the
+// device's primary context: after cudaDeviceReset (which unloads the library's
+// device code) it is stale, so a process that resets a device must not call
+// this entry point on that device again.
 //
 // Sharing: every call on a device uses the same array and finds the previous
 // call's contents in it; each call clears the part that must start at zero
-// (header and look-back words) on its own stream before launching.  Calls
+// (header and look-back words) on its own stream before launching, the first
+// call included, and the rank array is rewritten in full by every call.  Calls
 // that overlap on the GPU (different streams, or different host threads on
 // the same device) race on the array and must be serialised by the caller.
 // Device-side conditions (bad assignment, wait timeout) are recorded in the
 // array's header, which the next call clears; this entry point does not
-// report them.
+// report them.  After such a condition the outputs are not valid; a caller
+// that must detect it uses moe_b200_pack with its own workspace and reads
+// moe_b200_workspace_status.
 //
 // Nothing here calls cudaMalloc, cudaFree or any allocating routine.
 #include <mutex>
@@ -45,8 +51,8 @@ constexpr int kMaxDevices = 64;
 std::mutex g_setup_mutex;
 void* g_scratch_addr[kMaxDevices] = {};
 
-// Device address of the built-in scratch on the current device; looks it up
-// and zero-fills it on the first call per device.
+// Device address of the built-in scratch on the current device; looked up
+// on the first call per device.
 int scratch_on_current_device(void** out) {
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
@@ -59,8 +65,6 @@ int scratch_on_current_device(void** out) {
         void* p = nullptr;
         err = cudaGetSymbolAddress(&p, g_pack_noalloc_scratch);
         if (err != cudaSuccess) return moe_b200::cuda_fail(err, "pack_noalloc: cudaGetSymbolAddress");
-        err = cudaMemset(p, 0, MOE_B200_NOALLOC_SCRATCH_BYTES);
-        if (err != cudaSuccess) return moe_b200::cuda_fail(err, "pack_noalloc: zero-fill");
         g_scratch_addr[dev] = p;
     }
     *out = g_scratch_addr[dev];

@@ -115,11 +115,37 @@ unpermute_kernel(const uint4* __restrict__ y, const float* __restrict__ packed_w
 constexpr int kConsumerWarps = 8;
 constexpr int kBulkThreads = (kConsumerWarps + 1) * 32;
 
+// Expert parallel: the rows of y arrive from the peers; lanes of one warp
+// wait (bounded) until every rank's back flag reached the epoch, then order
+// the acquire before this thread's later bulk-copy reads of y.
+__device__ __forceinline__ void wait_back_flags(const EpWait& wt, int lane, uint32_t* dev_status) {
+    for (int i = lane; i < wt.n; i += 32) {
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire_sys(wt.flags + i) < wt.epoch) {
+            if (globaltimer_ns() - t0 > wt.timeout_ns) {
+                atomicOr(dev_status, MOE_B200_DEV_WAIT_TIMEOUT);
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    __syncwarp();
+    fence_proxy_async_global();
+}
+
+// Stand-alone form of the same wait, for the unpermute kernels that are not
+// bulk-copy pipelines.
+__global__ void ep_wait_back_kernel(EpWait wt, uint32_t* __restrict__ dev_status) {
+    pdl_wait_primary();
+    if (threadIdx.x < 32) wait_back_flags(wt, threadIdx.x, dev_status);
+    __threadfence_system();
+}
+
 template <int DT>
 __global__ void __launch_bounds__(kBulkThreads)
 unpermute_bulk_kernel(const uint16_t* __restrict__ y, const float* __restrict__ packed_w,
                       const int32_t* __restrict__ slot_pos, int T, int K, int d, int stages,
-                      uint4* __restrict__ out, uint32_t* __restrict__ dev_status) {
+                      uint4* __restrict__ out, uint32_t* __restrict__ dev_status, EpWait wt) {
     extern __shared__ __align__(128) unsigned char smem[];
     const uint32_t rowb = uint32_t(d) * 2;
     const size_t stage_bytes = size_t(K) * rowb;
@@ -149,6 +175,7 @@ unpermute_bulk_kernel(const uint16_t* __restrict__ y, const float* __restrict__ 
         const int gk = lane % K, gi = lane / K;
         const bool lane_used = gi < G;
         const int64_t n_mine = (T - 1 - int64_t(blockIdx.x)) / gridDim.x + 1;  // tokens of this CTA
+        if (wt.flags) wait_back_flags(wt, lane, dev_status);
         auto fetch_p = [&](int64_t g) -> int32_t {
             const int64_t i = g * G + gi;
             if (!lane_used || i >= n_mine) return -1;
@@ -271,7 +298,10 @@ static int bulk_smem_bytes(int K, int d, int stages) {
 }
 
 cudaError_t launch_unpermute(const void* y, const float* packed_w, const int32_t* slot_pos,
-                             int T, int K, int d, int dtype, void* out, cudaStream_t stream) {
+                             int T, int K, int d, int dtype, void* out, cudaStream_t stream,
+                             const EpWait* wait) {
+    EpWait wt{};
+    if (wait) wt = *wait;
     const bool vec = (d % 8 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0) &&
                      (reinterpret_cast<uintptr_t>(out) % 16 == 0);
     const int threads = 256;
@@ -301,7 +331,17 @@ cudaError_t launch_unpermute(const void* y, const float* packed_w, const int32_t
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
         return cudaLaunchKernelEx(&cfg, kern, static_cast<const uint16_t*>(y), packed_w, slot_pos, T, K,
-                                  d, stages, static_cast<uint4*>(out), st);
+                                  d, stages, static_cast<uint4*>(out), st, wt);
+    }
+    if (wt.flags) {
+        uint32_t* st = device_status_word();
+        if (!st) return cudaErrorInvalidDevice;
+        cudaLaunchConfig_t cfg = pdl_config(dim3(1), dim3(32), 0, stream);
+        cudaLaunchAttribute attr = pdl_attr();
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        cudaError_t err = cudaLaunchKernelEx(&cfg, ep_wait_back_kernel, wt, st);
+        if (err != cudaSuccess) return err;
     }
     if (vec) {
         const int warps_per_cta = threads / 32;

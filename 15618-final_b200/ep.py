@@ -24,14 +24,40 @@ def expert_ranges(E: int, N: int) -> List[int]:
     return bounds
 
 
-def balanced_labels(E: int, N: int) -> List[int]:
-    """Expert placement that deals experts round-robin over the ranks: expert e
-    (e = popularity rank, 0 = hottest) gets label first[e % N] + e // N, so
-    rank r owns labels [first[r], first[r+1]) = experts r, r+N, r+2N, ...
-    Routing with relabelled experts is the same as permuting the router's
-    output columns; packed rows stay grouped by owning rank."""
+def placement_owner(E: int, N: int) -> List[int]:
+    """Owner rank of every expert (e = popularity rank, 0 = hottest) under
+    the balanced placement: experts are dealt over the ranks in serpentine
+    order (0..N-1, then N-1..0, ...), skipping ranks whose label range
+    (expert_ranges) is full, so every rank gets one expert of each
+    popularity band and the bands alternate direction (under Zipf routing
+    the busiest rank's share drops below a plain round-robin deal's)."""
     b = expert_ranges(E, N)
-    return [b[e % N] + e // N for e in range(E)]
+    cap = [b[r + 1] - b[r] for r in range(N)]
+    owner = []
+    band = 0
+    while len(owner) < E:
+        order = range(N) if band % 2 == 0 else range(N - 1, -1, -1)
+        for r in order:
+            if len(owner) < E and cap[r] > 0:
+                owner.append(r)
+                cap[r] -= 1
+        band += 1
+    return owner
+
+
+def balanced_labels(E: int, N: int) -> List[int]:
+    """Expert placement for expert parallelism: expert e (popularity rank)
+    gets the next free label of rank placement_owner(E, N)[e], so rank r
+    owns labels [first[r], first[r+1]).  Routing with relabelled experts is
+    the same as permuting the router's output columns; packed rows stay
+    grouped by owning rank."""
+    b = expert_ranges(E, N)
+    nxt = list(b[:-1])
+    lab = []
+    for r in placement_owner(E, N):
+        lab.append(nxt[r])
+        nxt[r] += 1
+    return lab
 
 
 def owner_of(E: int, N: int) -> List[int]:
@@ -234,10 +260,25 @@ class FusedExpertParallel:
         p = self.L_.moe_b200_ep_recv_rows(self.ctx)
         return torch.as_tensor(_DeviceArray(p, (self.recv_cap, self.d), "<i2"), device=self.device).view(self.dtype)
 
+    def step(self, emb, asgn, wts, workspace, out, y, w_gate_up=None, w_down=None, h=None, stream=None):
+        """One whole step in ONE library call (moe_b200_ep_step): pack +
+        dispatch, receive, the expert (identity when no weights are given,
+        else the grouped SwiGLU with w_gate_up / w_down / h as ffn_return),
+        return and combine into y [T, d].  `out` is a moe_b200.PackResult
+        (packed unused)."""
+        T = emb.shape[0]
+        p = self.mb._ptr
+        I = 0 if w_down is None else w_down.shape[2]
+        self.mb._check(self.L_.moe_b200_ep_step(
+            self.ctx, p(emb), p(asgn), p(wts), T, I, p(w_gate_up), p(w_down), self.mb.dtype_code(self.dtype), p(h),
+            p(out.packed_weights), p(out.perm), p(out.expert_count), p(out.expert_start), p(out.slot_pos),
+            workspace.buf.data_ptr(), workspace.nbytes, p(y), self._s(stream)), "ep_step")
+        self.epoch = int(self.L_.moe_b200_ep_epoch(self.ctx))
+
     def dispatch(self, emb, asgn, wts, workspace, out, stream=None):
         """Starts a step: pack + peer-store dispatch.  `out` is a moe_b200.PackResult
         (its packed buffer is not written: rows go straight to their owners)."""
-        self.epoch += 1
+        self.epoch = max(self.epoch, int(self.L_.moe_b200_ep_epoch(self.ctx))) + 1
         T = emb.shape[0]
         p = self.mb._ptr
         self.mb._check(self.L_.moe_b200_ep_dispatch(

@@ -80,6 +80,10 @@ def lib() -> ctypes.CDLL:
                                                  vp, vp, vp]
     L.moe_b200_grouped_swiglu.restype = cint
     L.moe_b200_grouped_swiglu.argtypes = [vp, vp, vp, cint, cint, cint, cint, cint, vp, vp, cint, vp, vp, vp]
+    L.moe_b200_grouped_ffn.restype = cint
+    L.moe_b200_grouped_ffn.argtypes = [vp, vp, vp, cint, cint, cint, cint, cint, vp, vp, cint, vp, vp, vp]
+    L.moe_b200_ffn_weights_from_reference.restype = cint
+    L.moe_b200_ffn_weights_from_reference.argtypes = [vp, vp, cint, cint, cint, vp, vp, vp]
     L.moe_b200_router_weights_bytes.restype = sz
     L.moe_b200_router_weights_bytes.argtypes = [cint, cint, cint]
     L.moe_b200_router_prepare.restype = cint
@@ -118,6 +122,10 @@ def lib() -> ctypes.CDLL:
     L.moe_b200_ep_ffn_return.argtypes = [vp, u64, vp, vp, vp, vp, cint, vp, vp, cint, vp, vp]
     L.moe_b200_ep_combine.restype = cint
     L.moe_b200_ep_combine.argtypes = [vp, u64, vp, vp, cint, cint, vp, vp]
+    L.moe_b200_ep_step.restype = cint
+    L.moe_b200_ep_step.argtypes = [vp, vp, vp, vp, cint, cint, vp, vp, cint, vp, vp, vp, vp, vp, vp, vp, sz, vp, vp]
+    L.moe_b200_ep_epoch.restype = u64
+    L.moe_b200_ep_epoch.argtypes = [vp]
     L.moe_b200_unpermute.restype = cint
     L.moe_b200_unpermute.argtypes = [vp, vp, vp, cint, cint, cint, cint, vp, vp]
     _lib = L
@@ -362,6 +370,39 @@ def grouped_swiglu(x, seg_start, w_gate_up, w_down, seg_expert=None, h=None, y=N
                                          _ptr(w_gate_up), _ptr(w_down), dtype_code(x.dtype), _ptr(h), _ptr(y),
                                          _stream_handle(stream)), "grouped_swiglu")
     return h, y
+
+
+def grouped_ffn(x, seg_start, w_up, w_down, seg_expert=None, mid=None, y=None, stream=None):
+    """The reference's activation-free expert FFN, grouped, on packed rows
+    x [rows, d]: mid = x . w_up[e]^T, y = mid . w_down[e]^T (fp32 accumulate,
+    each rounded once).  w_up [E, F, d], w_down [E, d, F] (K-major; see
+    ffn_weights_from_reference).  Returns (mid [rows, F], y [rows, d])."""
+    import torch
+    rows, d = x.shape
+    E, F, _ = w_up.shape
+    nseg = seg_start.numel() - 1
+    if mid is None:
+        mid = torch.empty((rows, F), dtype=x.dtype, device=x.device)
+    if y is None:
+        y = torch.empty((rows, d), dtype=x.dtype, device=x.device)
+    _check(lib().moe_b200_grouped_ffn(_ptr(x), _ptr(seg_start), _ptr(seg_expert), nseg, rows, d, F, E, _ptr(w_up),
+                                      _ptr(w_down), dtype_code(x.dtype), _ptr(mid), _ptr(y), _stream_handle(stream)),
+           "grouped_ffn")
+    return mid, y
+
+
+def ffn_weights_from_reference(w1, w2, stream=None):
+    """The reference's expert weights W1 [E, d, F] / W2 [E, F, d] (row-major
+    B operands, apps/bench_e2e.cu:281-292) in the layout grouped_ffn takes:
+    (w_up [E, F, d], w_down [E, d, F]), transposed on the device."""
+    import torch
+    E, d, F = w1.shape
+    w_up = torch.empty((E, F, d), dtype=w1.dtype, device=w1.device)
+    w_down = torch.empty((E, d, F), dtype=w1.dtype, device=w1.device)
+    _check(lib().moe_b200_ffn_weights_from_reference(_ptr(w1.contiguous()), _ptr(w2.contiguous()), E, d, F,
+                                                     _ptr(w_up), _ptr(w_down), _stream_handle(stream)),
+           "ffn_weights_from_reference")
+    return w_up, w_down
 
 
 class RouterWeights:

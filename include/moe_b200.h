@@ -115,8 +115,12 @@ int moe_b200_workspace_status(void* workspace, size_t workspace_bytes, void* str
  * exceeds MOE_B200_NOALLOC_SCRATCH_BYTES are rejected with
  * MOE_B200_ERR_WORKSPACE (e.g. T*K above ~1M slots).
  *  - The first call on each device, made with that device current, looks up
- *    the array's address and zero-fills it (blocking); make that first call
- *    before any stream capture.
+ *    the array's address (a host-side lookup, nothing is enqueued); make that
+ *    first call before any stream capture.  The address is remembered per
+ *    device: after cudaDeviceReset it is stale, so do not call this entry
+ *    point on a device the process has reset.
+ *  - Every call clears the part of the array that must start at zero on its
+ *    own stream before its kernels run.
  *  - All calls on a device share the array: calls that overlap on the GPU
  *    race and must be serialised by the caller.
  *  - Device-side conditions (MOE_B200_DEV_*) are not reported by this entry
@@ -204,6 +208,27 @@ int moe_b200_grouped_swiglu_gather(const void* x_tokens, int T, const int32_t* r
                                    int rows, int d, int I, int E, const void* w_gate_up,
                                    const void* w_down, int dtype, void* h, void* y, void* stream);
 
+/* The reference's expert, activation-free, on the same grouped tcgen05
+ * kernel:  mid[r] = round16(x[r] . Wup[e]^T),  y[r] = round16(mid[r] . Wdown[e]^T),
+ * fp32 accumulation, for each row r of segment s (e = seg_expert[s], or s).
+ *   w_up   [E, F, d]   K-major up-projection (row j = inner feature j)
+ *   w_down [E, d, F]   K-major down-projection (row c = output column c)
+ *   mid    [rows, F]   out: the intermediate; y [rows, d] out
+ * d and F multiples of 16; pointers 16-byte aligned; nseg <= 1024.
+ * Replaces the per-expert cublasHgemm up/down loop (apps/bench_e2e.cu:274-301,
+ * apps/bench_prefill.cu:854-884), which needs the expert counts on the host;
+ * that loop's d_ffn is F.  Device-side conditions: moe_b200_device_status(). */
+int moe_b200_grouped_ffn(const void* x, const int32_t* seg_start, const int32_t* seg_expert,
+                         int nseg, int rows, int d, int F, int E, const void* w_up,
+                         const void* w_down, int dtype, void* mid, void* y, void* stream);
+
+/* One-time conversion of the reference's expert weights into the layout
+ * above: w1 [E, d, F] (the reference's d_W1, row-major B of mid = A . W1,
+ * apps/bench_e2e.cu:281-292) -> w_up [E, F, d]; w2 [E, F, d] (d_W2) ->
+ * w_down [E, d, F].  16-bit words, enqueued on `stream`; E <= 65535.        */
+int moe_b200_ffn_weights_from_reference(const void* w1, const void* w2, int E, int d, int F,
+                                        void* w_up, void* w_down, void* stream);
+
 /* ----------------------------------------------------- expert parallel ---- */
 
 /* Exchange layout of rank `rank` among `nranks` expert-parallel ranks, on the
@@ -235,9 +260,10 @@ int moe_b200_ep_layout(const int32_t* all_counts, int nranks, int E, int rank,
  *   all nranks handles in rank order -> steps -> barrier -> moe_b200_ep_destroy.
  * A step, with the same epoch on every rank (1, 2, 3, ...), enqueued on one
  * stream and never blocking the host:
- *   moe_b200_ep_dispatch         route/scan, publish counts to every peer,
- *                                 store every token row straight into the
- *                                 receive buffer of the rank owning its expert
+ *   moe_b200_ep_dispatch         route/scan (whose last tile publishes the
+ *                                 counts to every peer), then store every
+ *                                 token row straight into the receive buffer
+ *                                 of the rank owning its expert
  *   moe_b200_ep_receive           wait for all senders; segment table of the
  *                                 receive buffer (seg_* arrays of
  *                                 nranks*L' + H (+1) entries: L' = this rank's
@@ -247,6 +273,7 @@ int moe_b200_ep_layout(const int32_t* all_counts, int nranks, int E, int rank,
  *                                 the sender's back buffer
  *     or moe_b200_ep_return_identity   (identity expert)
  *   moe_b200_ep_combine           wait for all returns; weighted unpermute
+ * or all of it with one call, moe_b200_ep_step.
  * Replaces the reference's AllGather -> D2H -> host offsets -> grouped
  * ncclSend/ncclRecv dispatch and combine (apps/bench_prefill.cu:768-807,
  * 889-906).  Waits are bounded by timeout_ms and report
@@ -285,6 +312,22 @@ int moe_b200_ep_ffn_return(void* ctx, uint64_t epoch, const int32_t* seg_start,
                            const void* w_down, int dtype, void* h, void* stream);
 int moe_b200_ep_combine(void* ctx, uint64_t epoch, const float* packed_weights,
                         const int32_t* slot_pos, int T, int dtype, void* out, void* stream);
+
+/* One whole step in one call: dispatch -> receive -> expert -> combine with
+ * the next epoch (moe_b200_ep_epoch(ctx) + 1), five kernel launches for the
+ * identity expert (w_gate_up = w_down = NULL; I and h unused) and six for the
+ * grouped SwiGLU (w_gate_up / w_down / h as moe_b200_ep_ffn_return).  The
+ * segment table lives in the context.  Arguments otherwise as the stage
+ * calls; out [T, d] receives the combined rows.  Replaces one round of
+ * apps/bench_prefill.cu:768-906 (count all-gather, host offsets, dispatch
+ * AllToAllv, per-expert GEMMs, combine AllToAllv).                        */
+int moe_b200_ep_step(void* ctx, const void* emb, const int32_t* asgn, const float* wts, int T,
+                     int I, const void* w_gate_up, const void* w_down, int dtype, void* h,
+                     float* packed_weights, int32_t* perm, int32_t* expert_count,
+                     int32_t* expert_start, int32_t* slot_pos, void* workspace,
+                     size_t workspace_bytes, void* out, void* stream);
+/* Largest epoch enqueued on this context so far (0 before the first step). */
+uint64_t moe_b200_ep_epoch(void* ctx);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -24,7 +24,10 @@
  * at K = 2 (two fp32 atomic adds onto zero commute exactly) bit for bit, the
  * probabilities, assignments and K = 4 combine within stated bounds.  The
  * SwiGLU expert stays "unpinned" (no reference counterpart): it rests on
- * torch fp32 cross-checks.
+ * torch fp32 cross-checks.  oracle_plain_expert() restates the reference's
+ * activation-free expert and is pinned against outputs of the reference's
+ * own GPU layer (run_e2e, apps/bench_e2e.cu:218-329, compiled unchanged into
+ * oracle/_ref/libref_gpu.so) in tests/test_ref_gpu_golden.py.
  *
  * All 16-bit payloads are opaque uint16 words; dtype 0 = fp16, 1 = bf16.
  */
@@ -294,6 +297,38 @@ void oracle_swiglu_expert(const uint16_t* x, const uint16_t* w_gu, const uint16_
         }
     }
     free(xf); free(hf); free(wrow); free(gacc); free(uacc);
+}
+
+/* One activation-free expert on M rows: the reference's FFN (per-expert
+ * cublasHgemm up then down, apps/bench_e2e.cu:274-301) restated with fp32
+ * products summed in double, each result rounded once to dtype.
+ *   x     [M, D]      rows (dtype)
+ *   w_up  [F, D]      row j = inner feature j (the reference's W1[e] transposed)
+ *   w_dn  [D, F]      row n = output column n (the reference's W2[e] transposed)
+ *   mid   = x . w_up^T rounded to dtype, y = mid . w_dn^T rounded to dtype.
+ * Pinned against the reference's own GPU layer (tests/test_ref_gpu_golden.py). */
+void oracle_plain_expert(const uint16_t* x, const uint16_t* w_up, const uint16_t* w_dn, int M, int D, int F,
+                         int dtype, uint16_t* mid_out, uint16_t* y_out) {
+    float* xf = (float*)malloc(sizeof(float) * (size_t)D);
+    float* mf = (float*)malloc(sizeof(float) * (size_t)F);
+    for (int m = 0; m < M; ++m) {
+        for (int c = 0; c < D; ++c) xf[c] = to_f32(x[(size_t)m * D + c], dtype);
+        for (int j = 0; j < F; ++j) {
+            const uint16_t* ur = w_up + (size_t)j * D;
+            double acc = 0.0;
+            for (int c = 0; c < D; ++c) acc += (double)xf[c] * to_f32(ur[c], dtype);
+            const uint16_t mb = from_f32((float)acc, dtype);
+            if (mid_out) mid_out[(size_t)m * F + j] = mb;
+            mf[j] = to_f32(mb, dtype);
+        }
+        for (int n = 0; n < D; ++n) {
+            const uint16_t* dr = w_dn + (size_t)n * F;
+            double acc = 0.0;
+            for (int j = 0; j < F; ++j) acc += (double)mf[j] * to_f32(dr[j], dtype);
+            y_out[(size_t)m * D + n] = from_f32((float)acc, dtype);
+        }
+    }
+    free(xf); free(mf);
 }
 
 /* ------------------------------------------------------------------------ */

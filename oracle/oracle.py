@@ -157,6 +157,20 @@ def swiglu_expert(x, w_gu, w_dn, dtype):
     return h, y
 
 
+def plain_expert(x, w_up, w_dn, dtype):
+    """The reference's activation-free expert on rows x (uint16 [M, D]):
+    w_up [F, D], w_dn [D, F]; returns (mid [M, F], y [M, D]) uint16."""
+    x = _c(x, np.uint16)
+    w_up = _c(w_up, np.uint16)
+    w_dn = _c(w_dn, np.uint16)
+    M, D = x.shape
+    F = w_up.shape[0]
+    mid = np.empty((M, F), np.uint16)
+    y = np.empty((M, D), np.uint16)
+    lib().oracle_plain_expert(_p(x), _p(w_up), _p(w_dn), M, D, F, dtype, _p(mid), _p(y))
+    return mid, y
+
+
 def route(emb, w_gate, K, dtype, mode=1):
     """Router oracle: emb uint16 [T, d], w_gate float32 [d, E].  mode 0 = the
     reference's float arithmetic, mode 1 = double.  Returns (assignments

@@ -7,7 +7,8 @@
 // fused_route_kernel, unpack_combine_kernel, f32_to_f16_kernel), so the app
 // source is compiled UNCHANGED inside this translation unit (its main()
 // renamed) and the launchers below use the reference's own launch shapes
-// (apps/bench_e2e.cu:235-255 for the routers, :304-313 for the combine).
+// (apps/bench_e2e.cu:235-255 for the routers, :304-313 for the combine), and
+// the whole run_e2e layer is exported for expert-FFN golden vectors.
 // Built by `make -C oracle ref-gpu` into oracle/_ref/libref_gpu.so together
 // with the unchanged reference library sources the app links
 // (Makefile:97-98 of the reference).
@@ -125,6 +126,52 @@ int ref_gpu_unpack_combine(const std::uint16_t* y, const float* packed_w, const 
     if (!e) e = to_host(out32, d_out32, (std::size_t)T * d);
     if (!e) e = to_host(reinterpret_cast<__half*>(out16), d_out16, (std::size_t)T * d);
     cudaFree(d_y); cudaFree(d_pw); cudaFree(d_perm); cudaFree(d_out32); cudaFree(d_out16);
+    return (int)e;
+}
+
+// The reference's whole single-GPU MoE layer, run_e2e (apps/bench_e2e.cu:
+// 218-329) unchanged: router (fused_route_kernel when fused != 0, else the
+// gate/softmax/top-K chain), the IScatter strategy `strategy` from the
+// reference's own factory (src/scatter/factory.cu), the per-expert
+// cublasHgemm up/down loop with d_ffn = p.d_ffn, and the atomic combine.
+// Buffers come from the app's allocate_e2e (:192-215).  Inputs: emb [T, d]
+// fp16, w_gate [d, E] fp32, w1 [E, d, F] and w2 [E, F, d] fp16.  Outputs
+// (host): assignments / routing weights [T, K], perm / packed weights [T*K],
+// expert start / count [E], the expert intermediate mid [T*K, F], the expert
+// outputs y [T*K, d] in packed order and the combined output [T, d].
+int ref_gpu_moe_layer(const std::uint16_t* emb, const float* w_gate, const std::uint16_t* w1,
+                      const std::uint16_t* w2, int T, int K, int E, int d, int F, const char* strategy, int fused,
+                      std::int32_t* asgn, float* rwt, std::int32_t* perm, float* packed_w,
+                      std::int32_t* expert_start, std::int32_t* expert_count, std::uint16_t* mid,
+                      std::uint16_t* y, std::uint16_t* out) {
+    moe::MoEParams p{T, K, E, d, F};
+    const std::size_t TK = (std::size_t)T * K;
+    auto scatter = moe::make_scatter(strategy);
+    if (!scatter) return (int)cudaErrorInvalidValue;
+    __half *d_emb = nullptr, *d_w1 = nullptr, *d_w2 = nullptr;
+    float* d_gate = nullptr;
+    cudaError_t e = to_dev(&d_emb, reinterpret_cast<const __half*>(emb), (std::size_t)T * d);
+    if (!e) e = to_dev(&d_gate, w_gate, (std::size_t)d * E);
+    if (!e) e = to_dev(&d_w1, reinterpret_cast<const __half*>(w1), (std::size_t)E * d * F);
+    if (!e) e = to_dev(&d_w2, reinterpret_cast<const __half*>(w2), (std::size_t)E * F * d);
+    if (e) return (int)e;
+    cublasHandle_t cublas;
+    if (cublasCreate(&cublas) != CUBLAS_STATUS_SUCCESS) return (int)cudaErrorUnknown;
+    E2EBuffers b = allocate_e2e(p, scatter->workspace_bytes(p), /*naive=*/fused == 0);
+    run_e2e(d_emb, d_gate, d_w1, d_w2, p, fused != 0, *scatter, b, cublas, 0);
+    e = cudaDeviceSynchronize();
+    if (!e) e = to_host(asgn, b.d_asgn, TK);
+    if (!e) e = to_host(rwt, b.d_rwt, TK);
+    if (!e) e = to_host(perm, b.scatter_bufs.perm, TK);
+    if (!e) e = to_host(packed_w, b.scatter_bufs.packed_weights, TK);
+    if (!e) e = to_host(expert_start, b.scatter_bufs.expert_start, (std::size_t)E);
+    if (!e) e = to_host(expert_count, b.scatter_bufs.expert_count, (std::size_t)E);
+    if (!e) e = to_host(reinterpret_cast<__half*>(mid), b.d_ffn_tmp, TK * F);
+    if (!e) e = to_host(reinterpret_cast<__half*>(y), b.d_expert_out, TK * d);
+    if (!e) e = to_host(reinterpret_cast<__half*>(out), b.d_output, (std::size_t)T * d);
+    b.free();
+    cublasDestroy(cublas);
+    cudaFree(d_emb); cudaFree(d_gate); cudaFree(d_w1); cudaFree(d_w2);
     return (int)e;
 }
 

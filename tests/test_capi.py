@@ -169,3 +169,22 @@ def test_grouped_swiglu_rejects_bad_arguments_on_host():
     assert L.moe_b200_grouped_swiglu_gather(p, 0, p, p, None, 4, 64, 64, 32, 4, p, p, mb.BF16, p, p,
                                             None) == mb.ERR_INVALID_ARG
     assert b"grouped_swiglu" in L.moe_b200_last_error()
+
+
+def _noalloc(T=16, K=2, E=4, d=8, dev=0x2000):
+    L = mb.lib()
+    f = L.moe_b200_pack_noalloc
+    vp, ci = ctypes.c_void_p, ctypes.c_int
+    f.argtypes = [vp, vp, vp, ci, ci, ci, ci, vp, vp, vp, vp, vp, vp, vp]
+    f.restype = ci
+    return f(dev, dev, dev, T, K, E, d, dev, dev, dev, dev, dev, None, None)
+
+
+def test_noalloc_rejects_bad_arguments_on_host():
+    """moe_b200_pack_noalloc's argument checks run before any CUDA call."""
+    assert _noalloc(T=-1) == mb.ERR_INVALID_ARG
+    assert _noalloc(K=0) == mb.ERR_INVALID_ARG
+    assert _noalloc(K=33) == mb.ERR_UNSUPPORTED
+    assert _noalloc(E=mb.MAX_EXPERTS + 1) == mb.ERR_UNSUPPORTED
+    assert _noalloc(T=1 << 20, K=8, E=64) == mb.ERR_WORKSPACE
+    assert b"built-in scratch" in mb.lib().moe_b200_last_error()

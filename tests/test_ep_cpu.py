@@ -159,8 +159,14 @@ def test_balanced_placement_is_a_permutation_that_spreads_load():
         lab = ep.balanced_labels(E, N)
         assert sorted(lab) == list(range(E))
         b = ep.expert_ranges(E, N)
-        for e in range(E):  # expert e lands on rank e % N
-            assert b[e % N] <= lab[e] < b[e % N + 1]
+        own = ep.placement_owner(E, N)
+        for e in range(E):  # expert e lands on its owner's label range
+            assert b[own[e]] <= lab[e] < b[own[e] + 1]
+        # serpentine bands: the first N experts go to ranks 0..N-1, the next
+        # N (where every rank still has room) to N-1..0
+        assert own[:N] == list(range(N))
+        if E >= 2 * N and all(b[r + 1] - b[r] >= 2 for r in range(N)):
+            assert own[N:2 * N] == list(range(N - 1, -1, -1))
     # Zipf routing: the hottest rank's share drops with the balanced placement
     E, N = 60, 8
     asgn, _ = routing.gen_routing(8192, 4, E, "zipf", seed=0)

@@ -43,7 +43,7 @@ def single_gpu_layer(x, a, w, E, wgu, wdn, identity):
     return mb.unpermute(y, r.packed_weights, r.slot_pos, T, K)
 
 
-def run_fused_steps(epx, x, a, w, E, wgu_local, wdn_local, I, identity, steps, device):
+def run_fused_steps(epx, x, a, w, E, wgu_local, wdn_local, I, identity, steps, device, one_call=False):
     T, K = a.shape
     d = x.shape[1]
     ws = mb.Workspace(T, K, E, device=device)
@@ -57,6 +57,13 @@ def run_fused_steps(epx, x, a, w, E, wgu_local, wdn_local, I, identity, steps, d
     res = []
     for _ in range(steps):
         y = torch.empty((T, d), dtype=x.dtype, device=device)
+        if one_call:  # moe_b200_ep_step: the whole step in one library call
+            if identity:
+                epx.step(x, a, w, ws, out, y)
+            else:
+                epx.step(x, a, w, ws, out, y, wgu_local, wdn_local, h)
+            res.append(y)
+            continue
         epx.dispatch(x, a, w, ws, out)
         epx.receive()
         if identity:
@@ -69,9 +76,10 @@ def run_fused_steps(epx, x, a, w, E, wgu_local, wdn_local, I, identity, steps, d
     return res, ws
 
 
+@pytest.mark.parametrize("one_call", [False, True])
 @pytest.mark.parametrize("replicated", [(), (0, 3, 5), tuple(range(16))])  # none / some / every expert
 @pytest.mark.parametrize("identity", [True, False])
-def test_fused_ep_single_rank_matches_single_gpu_layer(cuda, identity, replicated):
+def test_fused_ep_single_rank_matches_single_gpu_layer(cuda, identity, replicated, one_call):
     T, K, E, d, I = 2048, 4, 16, 256, 128
     dtype = torch.bfloat16
     asgn, wts = routing.gen_routing(T, K, E, "zipf", seed=3)
@@ -85,7 +93,7 @@ def test_fused_ep_single_rank_matches_single_gpu_layer(cuda, identity, replicate
         assert sorted(loc) == list(range(E))
         assert loc[len(loc) - len(replicated):] == sorted(replicated)
         outs, ws = run_fused_steps(epx, x, a, w, E, wgu[loc].contiguous(), wdn[loc].contiguous(), I, identity, 3,
-                                   "cuda")
+                                   "cuda", one_call=one_call)
         assert mb.device_status() == 0
         assert ws.device_status() == 0
         want = single_gpu_layer(x, a, w, E, wgu, wdn, identity)
@@ -113,6 +121,19 @@ def test_fused_ep_wait_times_out_and_reports(cuda):
         outs, _ = run_fused_steps(epx, x, a, w, E, None, None, 0, True, 1, "cuda")
         assert mb.device_status() == 0
         ref = (w.sum(1, keepdim=True) * x.float())
+        torch.testing.assert_close(outs[0].float(), ref, rtol=1e-3, atol=1e-3)
+        # the back-flag wait inside the unpermute kernel: nobody returns rows
+        # for epoch 20, so its copy warp gives up and reports
+        pw = torch.full((T * K,), 0.5, dtype=torch.float32, device="cuda")
+        sp = torch.arange(T * K, dtype=torch.int32, device="cuda")
+        y = torch.empty((T, d), dtype=torch.float16, device="cuda")
+        epx.epoch = 20
+        epx.combine(pw, sp, T, y)
+        assert mb.device_status() & mb.DEV_WAIT_TIMEOUT
+        assert mb.device_status() == 0
+        # and a one-call step still works afterwards
+        outs, _ = run_fused_steps(epx, x, a, w, E, None, None, 0, True, 1, "cuda", one_call=True)
+        assert mb.device_status() == 0
         torch.testing.assert_close(outs[0].float(), ref, rtol=1e-3, atol=1e-3)
     finally:
         epx.close()
@@ -163,11 +184,13 @@ def _multi_worker(rank, world, port, results):
             for identity in (True, False):
                 epx = ep.FusedExpertParallel(E, K, d, T, dtype, device=dev, timeout_ms=5000, replicated=replicated)
                 loc = epx.local_experts
-                outs, _ = run_fused_steps(epx, x, a, w, E, wgu[loc].contiguous(), wdn[loc].contiguous(), I,
-                                          identity, 3, dev)
                 want = single_gpu_layer(x, a, w, E, wgu, wdn, identity)
                 key = (identity, len(replicated))
-                ok[key] = all(torch.equal(y.view(torch.int16), want.view(torch.int16)) for y in outs)
+                for one_call in (False, True):   # stage calls, then moe_b200_ep_step, on one context
+                    outs, _ = run_fused_steps(epx, x, a, w, E, wgu[loc].contiguous(), wdn[loc].contiguous(), I,
+                                              identity, 3, dev, one_call=one_call)
+                    ok[key + (one_call,)] = all(torch.equal(y.view(torch.int16), want.view(torch.int16))
+                                                for y in outs)
                 ok[("status",) + key] = mb.device_status()
                 epx.close()
         results[rank] = ok
@@ -191,5 +214,6 @@ def test_fused_ep_multi_gpu_matches_single_gpu():
     for r in range(world):
         for nrep in (0, 3):
             for identity in (True, False):
-                assert res[r][(identity, nrep)], res
+                for one_call in (False, True):
+                    assert res[r][(identity, nrep, one_call)], res
                 assert res[r][("status", identity, nrep)] == 0, res
