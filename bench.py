@@ -1057,8 +1057,11 @@ def gpu_arm(args):
         if world > 1:
             send, recv = exchange_bytes(res, world)
             worst = max(max(send), max(recv))
-            t_disp = stg["pack"]                  # route_scan + dispatch, max over ranks
-            t_ret = stg["expert"]                 # identity return (or FFN + return), max over ranks
+            if res["fused"]:
+                t_disp = stg["pack"]              # route_scan + dispatch, max over ranks
+                t_ret = stg["expert"]             # identity return (or FFN + return), max over ranks
+            else:                                 # NCCL: both AllToAllv (+ counts, D2H) in one stage
+                t_disp = t_ret = stg["mid"] / 2
             gbs = worst / (t_disp / 1e3) / 1e9
             line["ep"] = {
                 "experts_per_rank": [res["bounds"][g + 1] - res["bounds"][g] for g in range(world)],
@@ -1076,7 +1079,10 @@ def gpu_arm(args):
             }
             if not layer:
                 line["roofline"] = {
-                    "bound": "nvlink", "kernel": "ep_pack_dispatch_kernel (+ route_scan_kernel before it)",
+                    "bound": "nvlink",
+                    "kernel": ("ep_pack_dispatch_kernel (+ route_scan_kernel before it)" if res["fused"] else
+                               "NCCL all_to_all_single (half of the dispatch + combine stage, which also holds "
+                               "the count all-gather and the D2H of the split sizes)"),
                     "achieved": gbs, "peak": NVLINK_GBS, "unit": "GB/s", "frac": gbs / NVLINK_GBS,
                     "peak_source": "measured peer copy per direction on this pool's B200s (profiling recipe); "
                                    "900 GB/s nominal",

@@ -74,7 +74,9 @@ def fixture(ref_dir, prefix, keep_cols):
 
 
 def main():
-    ref_dir = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref_dir = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MOE_REFERENCE_DIR", "")
+    if not ref_dir:
+        raise SystemExit("give the reference tree as an argument or in MOE_REFERENCE_DIR")
     if not oracle.ref_available():
         sys.exit("oracle/_ref/libref_cpu.so missing: run `make -C oracle ref` first")
     mini()
