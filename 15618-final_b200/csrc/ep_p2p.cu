@@ -26,7 +26,7 @@
 //      flag = e on every peer
 //   5. unpermute (unpermute.cu): its copy warps wait for all back flags, then
 //      combine the local back buffer
-// // Replicated ("hot") experts: every rank holds its own copy of the experts in
+// Replicated ("hot") experts: every rank holds its own copy of the experts in
 // a set H (the same on all ranks, moe_b200_ep_set_replicated); a row routed
 // to an expert of H never leaves its rank: the dispatch stores it into a local
 // block after the senders' blocks of the own receive buffer, and the expert
@@ -123,6 +123,16 @@ __device__ bool wait_flags(const uint64_t* flags, int n, uint64_t epoch, uint64_
     return *s_fail == 0;
 }
 
+// ld_nc_v4 as a volatile asm statement, so it keeps its place before the
+// (volatile) row stores that follow it in program order.
+__device__ __forceinline__ uint4 ld_nc_v4_first(const uint4* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
 // Warp per token: row read once (16-byte loads), stored to the receive buffer
 // of the rank owning each slot's expert.
 __global__ void __launch_bounds__(256)
@@ -212,7 +222,7 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
 #pragma unroll
             for (int j = 0; j < VPL; ++j) {
                 const int i = c0 + j * 32 + lane;
-                v[j] = i < nvec ? ld_nc_v4(src + i) : make_uint4(0, 0, 0, 0);
+                v[j] = i < nvec ? ld_nc_v4_first(src + i) : make_uint4(0, 0, 0, 0);
             }
             for (int k = 0; k < K; ++k) {
                 uint4* dst = reinterpret_cast<uint4*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(dst_lane), k));
@@ -307,19 +317,38 @@ ep_receive_kernel(EpGeom g, char* const* __restrict__ peer, uint64_t epoch, int3
 // Rows are taken round-robin over the senders (row i of sender q % N for
 // q = 0, 1, ...), so at any moment the GPU's stores go to all peers at once
 // instead of every GPU writing to the same peer (measured on NVSwitch: 389
-// GB/s per GPU with destination-major order, 637 GB/s interleaved).
+// GB/s per GPU with destination-major order, 637 GB/s interleaved).  The
+// segment table sits in shared memory (the per-row segment search makes no
+// global round trips) and each lane loads its whole share of a row into
+// registers before storing any of it (a store to a peer pointer could alias
+// the source, so the compiler would otherwise serialise every load behind
+// the previous store).
+constexpr int kReturnVPL = 8;  // 16-byte vectors per lane per pass: 4 KB rows in one pass
+
 __global__ void __launch_bounds__(256)
 ep_return_identity_kernel(EpGeom g, char* const* __restrict__ back, const uint4* __restrict__ recv,
                           const int32_t* __restrict__ seg_start, const int32_t* __restrict__ seg_src,
                           const int32_t* __restrict__ seg_dst_row, int nseg, EpSignal sig) {
-    pdl_wait_primary();
+    extern __shared__ int32_t s_tab[];                // [nseg + 1] starts, [nseg] src, [nseg] dst row
+    int32_t* t_start = s_tab;
+    int32_t* t_src = s_tab + nseg + 1;
+    int32_t* t_dst = t_src + nseg;
     __shared__ int64_t s_lo[kEpMaxRanks + 2];
     __shared__ int64_t s_max;
+    pdl_wait_primary();
+    for (int i = threadIdx.x; i <= nseg; i += blockDim.x) {
+        t_start[i] = seg_start[i];
+        if (i < nseg) {
+            t_src[i] = seg_src[i];
+            t_dst[i] = seg_dst_row[i];
+        }
+    }
+    __syncthreads();
     // blocks q < N: the rows sender q sent (segments [q*L, (q+1)*L));
     // block N: this rank's own rows of the replicated experts
     const int N = g.nranks, L = g.lrange, NB = N + 1;
-    if (threadIdx.x <= N) s_lo[threadIdx.x] = seg_start[threadIdx.x * L];
-    if (threadIdx.x == 0) s_lo[NB] = seg_start[nseg];
+    if (threadIdx.x <= N) s_lo[threadIdx.x] = t_start[threadIdx.x * L];
+    if (threadIdx.x == 0) s_lo[NB] = t_start[nseg];
     __syncthreads();
     if (threadIdx.x == 0) {
         int64_t m = 0;
@@ -339,13 +368,25 @@ ep_return_identity_kernel(EpGeom g, char* const* __restrict__ back, const uint4*
         int lo = snd * L, hi = (snd < N ? lo + L : nseg) - 1;   // segment of this row within its block
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
-            if (seg_start[mid] <= row) lo = mid;
+            if (t_start[mid] <= row) lo = mid;
             else hi = mid - 1;
         }
-        const int64_t drow = int64_t(seg_dst_row[lo]) + (row - seg_start[lo]);
-        uint4* dst = reinterpret_cast<uint4*>(back[seg_src[lo]]) + drow * nvec;
+        const int64_t drow = int64_t(t_dst[lo]) + (row - t_start[lo]);
+        uint4* dst = reinterpret_cast<uint4*>(back[t_src[lo]]) + drow * nvec;
         const uint4* src = recv + row * nvec;
-        for (int i = lane; i < nvec; i += 32) st_v4(dst + i, ld_nc_v4(src + i));
+        for (int c0 = 0; c0 < nvec; c0 += 32 * kReturnVPL) {
+            uint4 v[kReturnVPL];
+#pragma unroll
+            for (int j = 0; j < kReturnVPL; ++j) {
+                const int i = c0 + j * 32 + lane;
+                v[j] = i < nvec ? ld_nc_v4_first(src + i) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int j = 0; j < kReturnVPL; ++j) {
+                const int i = c0 + j * 32 + lane;
+                if (i < nvec) st_v4(dst + i, v[j]);
+            }
+        }
     }
     // the last CTA to finish raises the back flags of every sender
     __threadfence_system();
@@ -601,7 +642,15 @@ static int ep_enqueue_return_identity(EpContext* ctx, uint64_t epoch, const int3
                                       const int32_t* seg_src, const int32_t* seg_dst_row, cudaStream_t s) {
     const EpGeom& g = ctx->g;
     const int nseg = g.nranks * g.lrange + g.nhot;
-    cudaLaunchConfig_t cfg = pdl_config(dim3(sm_count_ep() * 4), dim3(256), 0, s);
+    const size_t smem = size_t(3 * nseg + 1) * sizeof(int32_t);
+    if (smem > 200 * 1024)
+        return fail(MOE_B200_ERR_UNSUPPORTED, "ep_return_identity: %d segments exceed the on-chip table", nseg);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(ep_return_identity_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             int(smem));
+        if (e != cudaSuccess) return cuda_fail(e, "ep_return_identity attribute");
+    }
+    cudaLaunchConfig_t cfg = pdl_config(dim3(sm_count_ep() * 4), dim3(256), smem, s);
     cudaLaunchAttribute attr = pdl_attr();
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
