@@ -6,7 +6,9 @@
 //   [counts flags | data flags | back flags]  one u64 epoch word per sender
 //   inbox  [N][E] int32        every rank's expert counts for this step
 //   recv   [N * max_tokens * K][d]   rows routed to this rank's experts,
-//                              sender-major then local-expert-major
+//                              expert-major (see below)
+//   ret    [N * max_tokens * K] int64  return address of every received row:
+//                              sender << 32 | the sender's packed row
 //   back   [max_tokens * K][d] this rank's rows after their expert, in its
 //                              own packed order
 // One step (epoch e, the same on all ranks; epochs only grow, so no flag is
@@ -28,13 +30,17 @@
 //      combine the local back buffer
 // Replicated ("hot") experts: every rank holds its own copy of the experts in
 // a set H (the same on all ranks, moe_b200_ep_set_replicated); a row routed
-// to an expert of H never leaves its rank: the dispatch stores it into a local
-// block after the senders' blocks of the own receive buffer, and the expert
-// returns it to the own back buffer.  Receive buffer of rank r:
-//   [sender 0: r's non-replicated experts] ... [sender N-1: same] [own rows
-//   of the replicated experts, expert-major]
+// to an expert of H never leaves its rank.  Receive buffer of rank r,
+// expert-major so that every local expert is ONE contiguous segment for the
+// grouped FFN (sender-major (sender, expert) pieces of a few dozen rows each
+// would waste most of every 128-row tile at 8 ranks):
+//   [r's 1st non-replicated expert: rows of sender 0, sender 1, ..., N-1]
+//   [r's 2nd non-replicated expert: ...] ... [own rows of the replicated
+//   experts, expert-major]
 // and r's local expert weights are ordered [non-replicated experts of its
-// range, ascending] + [replicated experts, ascending].
+// range, ascending] + [replicated experts, ascending].  Each received row's
+// return address travels with it (the dispatch stores it into `ret`), so the
+// return needs no per-sender table.
 // The host never waits inside a step.  This replaces the reference's
 // AllGather -> D2H -> host offsets -> grouped ncclSend/ncclRecv exchange
 // (apps/bench_prefill.cu:768-807, 889-906).  Every wait is bounded (the
@@ -58,9 +64,8 @@ cudaError_t launch_unpermute(const void* y, const float* packed_w, const int32_t
                              int d, int dtype, void* out, cudaStream_t stream, const EpWait* wait);
 int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* seg_expert, int nseg, int rows,
                         int d, int I, int E, const void* w_gate_up, const void* w_down, int dtype, void* h,
-                        void* y, cudaStream_t s, char* const* dst_base, const int32_t* seg_src,
-                        const int32_t* seg_dst_row, int seg_groups, int seg_group_len, const int32_t* gather_rows,
-                        int gather_T, const EpSignal* sig);
+                        void* y, cudaStream_t s, char* const* dst_base, const int64_t* row_ret,
+                        const int32_t* gather_rows, int gather_T, const EpSignal* sig);
 
 constexpr int kEpMaxRanks = 64;
 
@@ -73,7 +78,7 @@ struct EpGeom {
     uint32_t hot[kEpMaxExperts / 32];  // replicated experts (bit e)
     int nhot;                          // |H|
     int lrange;                        // experts of this rank's range that are not replicated
-    size_t off_cflag, off_dflag, off_bflag, off_count, off_inbox, off_recv, off_back, total;
+    size_t off_cflag, off_dflag, off_bflag, off_count, off_inbox, off_recv, off_ret, off_back, total;
     int64_t recv_cap;
     uint64_t timeout_ns;
 };
@@ -88,13 +93,8 @@ struct EpContext {
     char** back_dev = nullptr;   // device array: every rank's back buffer
     bool connected = false;
     uint64_t epoch = 0;          // largest epoch enqueued so far
-    int32_t* seg = nullptr;      // moe_b200_ep_step's segment table: 4 arrays of kEpMaxSegs
+    int32_t* seg = nullptr;      // moe_b200_ep_step's segment table: [E + 1] starts + [E] experts
 };
-
-// Segments of one rank's receive buffer: nranks * (its range experts) +
-// replicated experts <= 64 * 1024 + 1024 in the worst case; the table of
-// moe_b200_ep_step holds the common case and the entry point checks.
-constexpr int kEpMaxSegs = 4096;
 
 static size_t al4k(size_t x) { return (x + 4095) & ~size_t(4095); }
 
@@ -144,6 +144,7 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
                         uint64_t* __restrict__ status, size_t status_words, uint64_t epoch,
                         uint32_t* __restrict__ dev_status, int inbox_smem) {
     __shared__ int s_fail;
+    __shared__ int64_t s_hot_base;
     // per expert e: the rank whose receive buffer takes its rows, and the
     // receive row of packed position p there = s_dst[e] + p
     extern __shared__ int64_t s_dst[];                          // [E]
@@ -166,26 +167,30 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
         inbox = s_inbox;
     }
     const int32_t* own = inbox + size_t(g.rank) * g.E;  // this rank's counts
+    // Receiver r (thread r): its non-replicated experts in ascending order,
+    // each holding every sender's rows in sender order; this sender's rows of
+    // expert e start after all senders' rows of r's earlier experts and the
+    // rows of senders < rank of expert e.
     if (threadIdx.x < g.nranks) {
-        // receiver r: this sender's block follows the blocks of senders < rank;
-        // inside it, r's non-replicated experts in ascending order
         const int r = threadIdx.x;
         int64_t base = 0;
-        for (int s = 0; s < g.rank; ++s)
-            for (int e = g.first[r]; e < g.first[r + 1]; ++e)
-                if (!ep_is_hot(g, e)) base += inbox[s * g.E + e];
         for (int e = g.first[r]; e < g.first[r + 1]; ++e) {
             if (ep_is_hot(g, e)) continue;
+            int64_t before = 0, col = 0;
+            for (int s = 0; s < g.nranks; ++s) {
+                const int32_t c = inbox[s * g.E + e];
+                col += c;
+                before += s < g.rank ? c : 0;
+            }
             s_owner[e] = r;
-            s_dst[e] = base - expert_start[e];
-            base += own[e];
+            s_dst[e] = base + before - expert_start[e];
+            base += col;
         }
-    } else if (threadIdx.x == g.nranks && g.nhot > 0) {
-        // replicated experts: the local block after every sender's block
-        int64_t base = 0;
-        for (int s = 0; s < g.nranks; ++s)
-            for (int e = g.first[g.rank]; e < g.first[g.rank + 1]; ++e)
-                if (!ep_is_hot(g, e)) base += inbox[s * g.E + e];
+        if (r == g.rank) s_hot_base = base;  // this rank's replicated block follows
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && g.nhot > 0) {
+        int64_t base = s_hot_base;
         for (int e = 0; e < g.E; ++e) {
             if (!ep_is_hot(g, e)) continue;
             s_owner[e] = g.rank;
@@ -212,7 +217,11 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
                 perm[p] = int32_t(t);
                 if (packed_w) packed_w[p] = __ldg(wts + sidx);
                 const int owner = s_owner[e];
-                dst_lane = reinterpret_cast<uint4*>(peer[owner] + g.off_recv + size_t(s_dst[e] + p) * rowb);
+                const int64_t rrow = s_dst[e] + p;
+                dst_lane = reinterpret_cast<uint4*>(peer[owner] + g.off_recv + size_t(rrow) * rowb);
+                // the row's return address travels with it
+                reinterpret_cast<int64_t*>(peer[owner] + g.off_ret)[rrow] =
+                    (int64_t(g.rank) << 32) | int64_t(uint32_t(p));
             }
             if (slot_pos) slot_pos[sidx] = p;
         }
@@ -244,11 +253,12 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
 }
 
 // Receiver: wait for every sender's rows, then the segment table of the
-// receive buffer with the return address of each segment.
+// receive buffer: one segment per local expert (the range's non-replicated
+// experts with every sender's rows, then the own rows of the replicated
+// experts), seg_expert = the local expert index.
 __global__ void __launch_bounds__(256)
 ep_receive_kernel(EpGeom g, char* const* __restrict__ peer, uint64_t epoch, int32_t* __restrict__ seg_start,
-                  int32_t* __restrict__ seg_expert, int32_t* __restrict__ seg_src,
-                  int32_t* __restrict__ seg_dst_row, uint32_t* __restrict__ dev_status, int inbox_smem) {
+                  int32_t* __restrict__ seg_expert, uint32_t* __restrict__ dev_status, int inbox_smem) {
     extern __shared__ int32_t s_inbox[];  // [N][E] when inbox_smem
     __shared__ int s_fail;
     __shared__ int32_t warp_tot[8];
@@ -277,23 +287,19 @@ ep_receive_kernel(EpGeom g, char* const* __restrict__ peer, uint64_t epoch, int3
     }
     __syncthreads();
     const int L = g.lrange;
-    const int nseg = g.nranks * L + g.nhot;
+    const int nseg = L + g.nhot;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     for (int base = 0; base < nseg; base += blockDim.x) {
-        const int i = base + tid;
+        const int j = base + tid;
         int32_t v = 0;
-        if (i < nseg) {
-            // sender-major blocks of the range experts, then the own rows of
-            // the replicated experts
-            const bool tail = i >= g.nranks * L;
-            const int s = tail ? g.rank : i / L, j = tail ? L + (i - g.nranks * L) : i % L;
-            const int e_glob = s_local[j];
-            v = inbox[s * g.E + e_glob];
-            seg_expert[i] = j;
-            seg_src[i] = s;
-            int32_t before = 0;  // sender s's packed start of expert e_glob
-            for (int e = 0; e < e_glob; ++e) before += inbox[s * g.E + e];
-            seg_dst_row[i] = before;
+        if (j < nseg) {
+            const int e = s_local[j];
+            if (j < L) {
+                for (int s = 0; s < g.nranks; ++s) v += inbox[s * g.E + e];
+            } else {
+                v = inbox[g.rank * g.E + e];
+            }
+            seg_expert[j] = j;
         }
         int32_t incl = v;
 #pragma unroll
@@ -305,7 +311,7 @@ ep_receive_kernel(EpGeom g, char* const* __restrict__ peer, uint64_t epoch, int3
         __syncthreads();
         int32_t off = carry;
         for (int w = 0; w < warp; ++w) off += warp_tot[w];
-        if (i < nseg) seg_start[i] = off + incl - v;
+        if (j < nseg) seg_start[j] = off + incl - v;
         __syncthreads();
         if (tid == blockDim.x - 1) carry = off + incl;
         __syncthreads();
@@ -313,66 +319,33 @@ ep_receive_kernel(EpGeom g, char* const* __restrict__ peer, uint64_t epoch, int3
     if (tid == 0) seg_start[nseg] = carry;
 }
 
-// Identity expert: every received row goes back to its sender's back buffer.
-// Rows are taken round-robin over the senders (row i of sender q % N for
-// q = 0, 1, ...), so at any moment the GPU's stores go to all peers at once
-// instead of every GPU writing to the same peer (measured on NVSwitch: 389
-// GB/s per GPU with destination-major order, 637 GB/s interleaved).  The
-// segment table sits in shared memory (the per-row segment search makes no
-// global round trips) and each lane loads its whole share of a row into
-// registers before storing any of it (a store to a peer pointer could alias
-// the source, so the compiler would otherwise serialise every load behind
-// the previous store).
+// Identity expert: every received row goes back to its sender's back buffer,
+// at the return address the dispatch stored beside it.  Rows are visited in
+// a scattered order (row = q * kRowStride mod rows, a bijection because the
+// stride is a prime larger than any row count), so at any moment the GPU's
+// stores go to all senders at once instead of one sender's run of rows
+// (measured on NVSwitch: 389 GB/s per GPU when all GPUs store to one peer at
+// a time, 637 GB/s interleaved).  Each lane loads its whole share of a row
+// into registers before storing any of it (a store to a peer pointer could
+// alias the source, so the compiler would otherwise serialise every load
+// behind the previous store).
 constexpr int kReturnVPL = 8;  // 16-byte vectors per lane per pass: 4 KB rows in one pass
+constexpr int64_t kRowStride = 2147483647;  // 2^31 - 1, prime
 
 __global__ void __launch_bounds__(256)
 ep_return_identity_kernel(EpGeom g, char* const* __restrict__ back, const uint4* __restrict__ recv,
-                          const int32_t* __restrict__ seg_start, const int32_t* __restrict__ seg_src,
-                          const int32_t* __restrict__ seg_dst_row, int nseg, EpSignal sig) {
-    extern __shared__ int32_t s_tab[];                // [nseg + 1] starts, [nseg] src, [nseg] dst row
-    int32_t* t_start = s_tab;
-    int32_t* t_src = s_tab + nseg + 1;
-    int32_t* t_dst = t_src + nseg;
-    __shared__ int64_t s_lo[kEpMaxRanks + 2];
-    __shared__ int64_t s_max;
+                          const int64_t* __restrict__ ret, const int32_t* __restrict__ seg_start, int nseg,
+                          EpSignal sig) {
     pdl_wait_primary();
-    for (int i = threadIdx.x; i <= nseg; i += blockDim.x) {
-        t_start[i] = seg_start[i];
-        if (i < nseg) {
-            t_src[i] = seg_src[i];
-            t_dst[i] = seg_dst_row[i];
-        }
-    }
-    __syncthreads();
-    // blocks q < N: the rows sender q sent (segments [q*L, (q+1)*L));
-    // block N: this rank's own rows of the replicated experts
-    const int N = g.nranks, L = g.lrange, NB = N + 1;
-    if (threadIdx.x <= N) s_lo[threadIdx.x] = t_start[threadIdx.x * L];
-    if (threadIdx.x == 0) s_lo[NB] = t_start[nseg];
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int64_t m = 0;
-        for (int q = 0; q < NB; ++q) m = max(m, s_lo[q + 1] - s_lo[q]);
-        s_max = m;
-    }
-    __syncthreads();
+    const int64_t total = seg_start[nseg];
     const int nvec = g.d / 8;
     const int lane = threadIdx.x & 31;
-    const int64_t total = s_max * NB;
     const int64_t gw = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int64_t nw = int64_t(gridDim.x) * (blockDim.x >> 5);
     for (int64_t q = gw; q < total; q += nw) {
-        const int snd = int(q % NB);
-        const int64_t row = s_lo[snd] + q / NB;
-        if (row >= s_lo[snd + 1]) continue;
-        int lo = snd * L, hi = (snd < N ? lo + L : nseg) - 1;   // segment of this row within its block
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (t_start[mid] <= row) lo = mid;
-            else hi = mid - 1;
-        }
-        const int64_t drow = int64_t(t_dst[lo]) + (row - t_start[lo]);
-        uint4* dst = reinterpret_cast<uint4*>(back[t_src[lo]]) + drow * nvec;
+        const int64_t row = (q * kRowStride) % total;
+        const int64_t r = ret[row];
+        uint4* dst = reinterpret_cast<uint4*>(back[int(r >> 32)]) + int64_t(uint32_t(r)) * nvec;
         const uint4* src = recv + row * nvec;
         for (int c0 = 0; c0 < nvec; c0 += 32 * kReturnVPL) {
             uint4 v[kReturnVPL];
@@ -450,14 +423,15 @@ int moe_b200_ep_create(int nranks, int rank, int E, int K, int d, int max_tokens
     g.off_inbox = 4096;
     g.off_recv = g.off_inbox + al4k(size_t(nranks) * E * 4);
     g.recv_cap = int64_t(nranks) * max_tokens * K;
-    g.off_back = g.off_recv + al4k(size_t(g.recv_cap) * d * 2);
+    g.off_ret = g.off_recv + al4k(size_t(g.recv_cap) * d * 2);
+    g.off_back = g.off_ret + al4k(size_t(g.recv_cap) * 8);
     g.total = g.off_back + al4k(size_t(max_tokens) * K * d * 2);
     g.timeout_ns = uint64_t(timeout_ms) * 1000000ull;
     cudaError_t err = cudaGetDevice(&ctx->device);
     if (err == cudaSuccess) err = cudaMalloc(&ctx->region, g.total);
     if (err == cudaSuccess) err = cudaMemset(ctx->region, 0, g.total);
     if (err == cudaSuccess) err = cudaMalloc(&ctx->peer_dev, sizeof(char*) * kEpMaxRanks * 2);
-    if (err == cudaSuccess) err = cudaMalloc(&ctx->seg, sizeof(int32_t) * 4 * (kEpMaxSegs + 1));
+    if (err == cudaSuccess) err = cudaMalloc(&ctx->seg, sizeof(int32_t) * 2 * (size_t(E) + 1));
     if (err != cudaSuccess) {
         if (ctx->region) cudaFree(ctx->region);
         if (ctx->peer_dev) cudaFree(ctx->peer_dev);
@@ -619,15 +593,13 @@ static int ep_enqueue_dispatch(EpContext* ctx, uint64_t epoch, const void* emb, 
 }
 
 static int ep_enqueue_receive(EpContext* ctx, uint64_t epoch, int32_t* seg_start, int32_t* seg_expert,
-                              int32_t* seg_src, int32_t* seg_dst_row, cudaStream_t s) {
-    if (!seg_start || !seg_expert || !seg_src || !seg_dst_row)
-        return fail(MOE_B200_ERR_INVALID_ARG, "ep_receive: null segment buffer");
+                              cudaStream_t s) {
+    if (!seg_start || !seg_expert) return fail(MOE_B200_ERR_INVALID_ARG, "ep_receive: null segment buffer");
     uint32_t* st = device_status_word();
     if (!st) return fail(MOE_B200_ERR_CUDA, "ep_receive: device status word unavailable");
     const int inbox_smem = int64_t(ctx->g.nranks) * ctx->g.E <= kInboxSmemMax ? 1 : 0;
     const size_t smem = inbox_smem ? size_t(ctx->g.nranks) * ctx->g.E * 4 : 0;
-    ep_receive_kernel<<<1, 256, smem, s>>>(ctx->g, ctx->peer_dev, epoch, seg_start, seg_expert, seg_src,
-                                           seg_dst_row, st, inbox_smem);
+    ep_receive_kernel<<<1, 256, smem, s>>>(ctx->g, ctx->peer_dev, epoch, seg_start, seg_expert, st, inbox_smem);
     cudaError_t err = cudaGetLastError();
     return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "ep_receive launch");
 }
@@ -638,42 +610,34 @@ static EpSignal back_signal(EpContext* ctx, int which, uint64_t epoch) {
                     reinterpret_cast<uint32_t*>(ctx->region + g.off_count) + 2 * which, g.rank, g.nranks, epoch};
 }
 
-static int ep_enqueue_return_identity(EpContext* ctx, uint64_t epoch, const int32_t* seg_start,
-                                      const int32_t* seg_src, const int32_t* seg_dst_row, cudaStream_t s) {
+static int ep_enqueue_return_identity(EpContext* ctx, uint64_t epoch, const int32_t* seg_start, cudaStream_t s) {
     const EpGeom& g = ctx->g;
-    const int nseg = g.nranks * g.lrange + g.nhot;
-    const size_t smem = size_t(3 * nseg + 1) * sizeof(int32_t);
-    if (smem > 200 * 1024)
-        return fail(MOE_B200_ERR_UNSUPPORTED, "ep_return_identity: %d segments exceed the on-chip table", nseg);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(ep_return_identity_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             int(smem));
-        if (e != cudaSuccess) return cuda_fail(e, "ep_return_identity attribute");
-    }
-    cudaLaunchConfig_t cfg = pdl_config(dim3(sm_count_ep() * 4), dim3(256), smem, s);
+    const int nseg = g.lrange + g.nhot;
+    cudaLaunchConfig_t cfg = pdl_config(dim3(sm_count_ep() * 4), dim3(256), 0, s);
     cudaLaunchAttribute attr = pdl_attr();
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     cudaError_t err = cudaLaunchKernelEx(&cfg, ep_return_identity_kernel, g, static_cast<char* const*>(ctx->back_dev),
-                                         reinterpret_cast<const uint4*>(ctx->region + g.off_recv), seg_start, seg_src,
-                                         seg_dst_row, nseg, back_signal(ctx, 0, epoch));
+                                         reinterpret_cast<const uint4*>(ctx->region + g.off_recv),
+                                         reinterpret_cast<const int64_t*>(ctx->region + g.off_ret), seg_start, nseg,
+                                         back_signal(ctx, 0, epoch));
     return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "ep_return_identity launch");
 }
 
 static int ep_enqueue_ffn_return(EpContext* ctx, uint64_t epoch, const int32_t* seg_start,
-                                 const int32_t* seg_expert, const int32_t* seg_src, const int32_t* seg_dst_row,
-                                 int I, const void* w_gate_up, const void* w_down, int dtype, void* h,
-                                 cudaStream_t s) {
+                                 const int32_t* seg_expert, int I, const void* w_gate_up, const void* w_down,
+                                 int dtype, void* h, cudaStream_t s) {
     const EpGeom& g = ctx->g;
-    // GEMM 2's epilogue stores each finished tile straight into the back
-    // buffer of the rank that sent its rows (scatter mode); its last CTA
-    // raises the back flags.  Local experts: the range's non-replicated ones,
-    // then the replicated ones.
+    // GEMM 2's epilogue stores every finished row straight into the back
+    // buffer of the rank that sent it, at the return address stored beside
+    // the row (scatter mode); its last CTA raises the back flags.  One
+    // segment per local expert: the range's non-replicated ones, then the
+    // replicated ones.
     const EpSignal sig = back_signal(ctx, 1, epoch);
-    return grouped_swiglu_impl(ctx->region + g.off_recv, seg_start, seg_expert, g.nranks * g.lrange + g.nhot,
+    return grouped_swiglu_impl(ctx->region + g.off_recv, seg_start, seg_expert, g.lrange + g.nhot,
                                int(g.recv_cap), g.d, I, g.lrange + g.nhot, w_gate_up, w_down, dtype, h,
-                               ctx->region + g.off_recv, s, ctx->back_dev, seg_src, seg_dst_row, g.nranks, g.lrange,
-                               nullptr, 0, &sig);
+                               ctx->region + g.off_recv, s, ctx->back_dev,
+                               reinterpret_cast<const int64_t*>(ctx->region + g.off_ret), nullptr, 0, &sig);
 }
 
 static int ep_enqueue_combine(EpContext* ctx, uint64_t epoch, const float* packed_weights, const int32_t* slot_pos,
@@ -708,30 +672,26 @@ int moe_b200_ep_dispatch(void* c, uint64_t epoch, const void* emb, const int32_t
                                slot_pos, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
-int moe_b200_ep_receive(void* c, uint64_t epoch, int32_t* seg_start, int32_t* seg_expert, int32_t* seg_src,
-                        int32_t* seg_dst_row, void* stream) {
+int moe_b200_ep_receive(void* c, uint64_t epoch, int32_t* seg_start, int32_t* seg_expert, void* stream) {
     EpContext* ctx = connected_ctx(c, "ep_receive");
     if (!ctx) return MOE_B200_ERR_INVALID_ARG;
-    return ep_enqueue_receive(ctx, epoch, seg_start, seg_expert, seg_src, seg_dst_row,
-                              static_cast<cudaStream_t>(stream));
+    return ep_enqueue_receive(ctx, epoch, seg_start, seg_expert, static_cast<cudaStream_t>(stream));
 }
 
-int moe_b200_ep_return_identity(void* c, uint64_t epoch, const int32_t* seg_start, const int32_t* seg_src,
-                                const int32_t* seg_dst_row, void* stream) {
+int moe_b200_ep_return_identity(void* c, uint64_t epoch, const int32_t* seg_start, void* stream) {
     EpContext* ctx = connected_ctx(c, "ep_return_identity");
     if (!ctx) return MOE_B200_ERR_INVALID_ARG;
-    if (!seg_start || !seg_src || !seg_dst_row)
-        return fail(MOE_B200_ERR_INVALID_ARG, "ep_return_identity: null segment buffer");
-    return ep_enqueue_return_identity(ctx, epoch, seg_start, seg_src, seg_dst_row, static_cast<cudaStream_t>(stream));
+    if (!seg_start) return fail(MOE_B200_ERR_INVALID_ARG, "ep_return_identity: null segment buffer");
+    return ep_enqueue_return_identity(ctx, epoch, seg_start, static_cast<cudaStream_t>(stream));
 }
 
-int moe_b200_ep_ffn_return(void* c, uint64_t epoch, const int32_t* seg_start, const int32_t* seg_expert,
-                           const int32_t* seg_src, const int32_t* seg_dst_row, int I, const void* w_gate_up,
-                           const void* w_down, int dtype, void* h, void* stream) {
+int moe_b200_ep_ffn_return(void* c, uint64_t epoch, const int32_t* seg_start, const int32_t* seg_expert, int I,
+                           const void* w_gate_up, const void* w_down, int dtype, void* h, void* stream) {
     EpContext* ctx = connected_ctx(c, "ep_ffn_return");
     if (!ctx) return MOE_B200_ERR_INVALID_ARG;
-    return ep_enqueue_ffn_return(ctx, epoch, seg_start, seg_expert, seg_src, seg_dst_row, I, w_gate_up, w_down, dtype,
-                                 h, static_cast<cudaStream_t>(stream));
+    if (!seg_start || !seg_expert) return fail(MOE_B200_ERR_INVALID_ARG, "ep_ffn_return: null segment buffer");
+    return ep_enqueue_ffn_return(ctx, epoch, seg_start, seg_expert, I, w_gate_up, w_down, dtype, h,
+                                 static_cast<cudaStream_t>(stream));
 }
 
 int moe_b200_ep_combine(void* c, uint64_t epoch, const float* packed_weights, const int32_t* slot_pos, int T,
@@ -748,27 +708,20 @@ int moe_b200_ep_step(void* c, const void* emb, const int32_t* asgn, const float*
     EpContext* ctx = connected_ctx(c, "ep_step");
     if (!ctx) return MOE_B200_ERR_INVALID_ARG;
     const EpGeom& g = ctx->g;
-    const int nseg = g.nranks * g.lrange + g.nhot;
-    if (nseg > kEpMaxSegs)
-        return fail(MOE_B200_ERR_UNSUPPORTED, "ep_step: %d receive segments exceed %d; use the stage entry points",
-                    nseg, kEpMaxSegs);
     if (!packed_weights) return fail(MOE_B200_ERR_INVALID_ARG, "ep_step: packed_weights is required");
     const bool identity = w_gate_up == nullptr && w_down == nullptr;
     if (!identity && (!w_gate_up || !w_down || !h || I < 1))
         return fail(MOE_B200_ERR_INVALID_ARG, "ep_step: the FFN needs w_gate_up, w_down, h and I >= 1");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const uint64_t epoch = ctx->epoch + 1;
-    int32_t* seg_start = ctx->seg;
-    int32_t* seg_expert = seg_start + (kEpMaxSegs + 1);
-    int32_t* seg_src = seg_expert + (kEpMaxSegs + 1);
-    int32_t* seg_dst_row = seg_src + (kEpMaxSegs + 1);
+    int32_t* seg_start = ctx->seg;                  // [E + 1]
+    int32_t* seg_expert = seg_start + (g.E + 1);   // [E]
     int st = ep_enqueue_dispatch(ctx, epoch, emb, asgn, wts, T, packed_weights, perm, expert_count, expert_start,
                                  slot_pos, workspace, workspace_bytes, s);
-    if (st == MOE_B200_OK) st = ep_enqueue_receive(ctx, epoch, seg_start, seg_expert, seg_src, seg_dst_row, s);
+    if (st == MOE_B200_OK) st = ep_enqueue_receive(ctx, epoch, seg_start, seg_expert, s);
     if (st == MOE_B200_OK)
-        st = identity ? ep_enqueue_return_identity(ctx, epoch, seg_start, seg_src, seg_dst_row, s)
-                      : ep_enqueue_ffn_return(ctx, epoch, seg_start, seg_expert, seg_src, seg_dst_row, I, w_gate_up,
-                                              w_down, dtype, h, s);
+        st = identity ? ep_enqueue_return_identity(ctx, epoch, seg_start, s)
+                      : ep_enqueue_ffn_return(ctx, epoch, seg_start, seg_expert, I, w_gate_up, w_down, dtype, h, s);
     if (st == MOE_B200_OK) st = ep_enqueue_combine(ctx, epoch, packed_weights, slot_pos, T, dtype, out, s);
     return st;
 }

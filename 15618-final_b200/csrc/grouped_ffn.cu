@@ -161,11 +161,13 @@ __device__ __forceinline__ void stage_put(unsigned char* stg, int row, int chunk
                  : "memory");
 }
 
-// Writes the warp's staged 32 x 64 columns to dst rows 0..nrows-1 (columns
+// Writes the warp's staged 32 x 64 columns to its rows 0..nrows-1 (columns
 // col0 .. col0+63, clipped at n_out): 4 rows x 128 contiguous bytes per warp
-// store instruction instead of 32 scattered 16-byte pieces.
+// store instruction instead of 32 scattered 16-byte pieces.  Row r goes to
+// dst + r * stride, or, when lane_row is given (scatter mode), to the row
+// address lane r holds in lane_row.
 __device__ __forceinline__ void stage_flush(const unsigned char* stg, int lane, uint16_t* dst, int64_t stride,
-                                            int nrows, int col0, int n_out) {
+                                            int nrows, int col0, int n_out, uint16_t* lane_row) {
     __syncwarp();
     const int ch = lane & 7;
     const bool col_ok = col0 + ch * 8 < n_out;
@@ -177,7 +179,9 @@ __device__ __forceinline__ void stage_flush(const unsigned char* stg, int lane, 
                      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                      : "r"(smem_u32(stg + r * 128 + ((ch ^ (r & 7)) << 4)))
                      : "memory");
-        if (r < nrows && col_ok) st_v4(reinterpret_cast<uint4*>(dst + int64_t(r) * stride + col0) + ch, v);
+        uint16_t* row = dst ? dst + int64_t(r) * stride
+                            : reinterpret_cast<uint16_t*>(__shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(lane_row), r));
+        if (r < nrows && col_ok) st_v4(reinterpret_cast<uint4*>(row + col0) + ch, v);
     }
     __syncwarp();
 }
@@ -203,8 +207,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                     int nseg, int kdim, int b_rows_per_expert, int n_out, int n_blocks,
                     int gate_up_split, uint16_t* __restrict__ out, int64_t out_stride,
                     uint32_t* __restrict__ dev_status, char* const* __restrict__ dst_base,
-                    const int32_t* __restrict__ seg_src, const int32_t* __restrict__ seg_dst_row,
-                    int seg_groups, int seg_group_len, const int32_t* __restrict__ gather_rows,
+                    const int64_t* __restrict__ row_ret, const int32_t* __restrict__ gather_rows,
                     int gather_limit, EpSignal sig) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte aligned stage buffers (SW128 atoms), control block after them.
@@ -220,18 +223,14 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     FfnSmem* ctl = reinterpret_cast<FfnSmem*>(s_stage + kStageBytes);
     int32_t* blk_prefix = reinterpret_cast<int32_t*>(ctl + 1);  // [nseg + 1]
     int32_t* s_start = blk_prefix + (nseg + 1);                 // [nseg + 1] row offsets
-    // [nseg] expert of each segment (low 16 bits) | source rank << 16.  In
-    // scatter mode (dst_base != nullptr) row r of segment s is stored at
-    // dst_base[seg_src[s]] + (seg_dst_row[s] + r) rows -- e.g. the back buffer
-    // of the rank that sent the segment's rows
-    int32_t* s_expsrc = s_start + (nseg + 1);
-    int32_t* s_dst_row = s_expsrc + nseg;                       // [nseg]
+    // [nseg] expert of each segment.  In scatter mode (dst_base != nullptr)
+    // row i of the input (the receive buffer) is stored at row
+    // (row_ret[i] & 0xffffffff) of dst_base[row_ret[i] >> 32] -- the back
+    // buffer of the rank that sent it, at its packed position there
+    int32_t* s_exp = s_start + (nseg + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     volatile int* abort_flag = &ctl->abort_flag;
-    const int G = seg_groups > 1 ? seg_groups : 1;
-    const int Lg = G > 1 ? seg_group_len : 0;
-    const int GL = G * Lg;  // segments in the interleaved groups; later ones keep their order
     // CTA-pair coordinates (CG = 2): rank 0 is the leader that issues the MMAs.
     const uint32_t crank = CG == 2 ? cluster_rank() : 0u;
     const int tile0 = CG == 2 ? int(cluster_id_x()) : int(blockIdx.x);
@@ -251,13 +250,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         mbar_fence_init();
     }
     if (warp == 0) {
-        // Tiles walk the segments in "tile order": with seg_groups = G > 1 the
-        // first G * L segments (L = seg_group_len; stored group-major: group
-        // q, item j at q*L+j) are visited item-major (j*G + q), so consecutive
-        // row blocks share an expert and rotate over the groups (the senders,
-        // whose buffers the scatter epilogue writes to); segments after them
-        // keep their order.  blk_prefix[i] = row blocks of the segments
-        // before tile-order position i.
+        // blk_prefix[i] = row blocks of the segments before segment i
         int run = 0;
         for (int s0 = 0; s0 < nseg; s0 += 32) {
             int i = s0 + lane;
@@ -265,10 +258,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             if (i < nseg) {
                 const int lo = seg_start[i];
                 s_start[i] = lo;
-                s_expsrc[i] = (seg_expert ? seg_expert[i] : i) | (dst_base ? seg_src[i] << 16 : 0);
-                if (dst_base) s_dst_row[i] = seg_dst_row[i];
-                const int nat = i < GL ? (i % G) * Lg + i / G : i;  // segment at tile-order position i
-                const int rows = seg_start[nat + 1] - seg_start[nat];
+                s_exp[i] = seg_expert ? seg_expert[i] : i;
+                const int rows = seg_start[i + 1] - lo;
                 cnt = rows > 0 ? (rows + kBlockRows - 1) / kBlockRows : 0;
             }
             int incl = cnt;
@@ -325,10 +316,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         const int total_rows = s_start[nseg];
         for (int tile = tile0; tile < total_tiles && !*abort_flag; tile += tile_step) {
             const int g = tile / n_blocks, n = tile % n_blocks;
-            const int ti = find_segment(blk_prefix, nseg, g);
-            const int s = ti < GL ? (ti % G) * Lg + ti / G : ti;
-            const int e = s_expsrc[s] & 0xffff;
-            const int row0 = s_start[s] + (g - blk_prefix[ti]) * kBlockRows;
+            const int s = find_segment(blk_prefix, nseg, g);
+            const int e = s_exp[s];
+            const int row0 = s_start[s] + (g - blk_prefix[s]) * kBlockRows;
             int r4[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -366,10 +356,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             uint32_t it = 0;
             for (int tile = tile0; tile < total_tiles && !*abort_flag; tile += tile_step) {
                 const int g = tile / n_blocks, n = tile % n_blocks;
-                const int ti = find_segment(blk_prefix, nseg, g);
-                const int s = ti < GL ? (ti % G) * Lg + ti / G : ti;
-                const int e = s_expsrc[s] & 0xffff;
-                const int row0 = s_start[s] + (g - blk_prefix[ti]) * kBlockRows + int(crank) * kTileM;
+                const int s = find_segment(blk_prefix, nseg, g);
+                const int e = s_exp[s];
+                const int row0 = s_start[s] + (g - blk_prefix[s]) * kBlockRows + int(crank) * kTileM;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const int st = int(it % kStages);
                     if (!wait_or_abort(&ctl->empty[st], ((it / kStages) & 1u) ^ 1u, abort_flag, dev_status))
@@ -460,19 +449,20 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             if (!wait_or_abort(&ctl->tmem_full[buf], (j >> 1) & 1u, abort_flag, dev_status)) break;
             tc_fence_after();
             const int g = tile / n_blocks, n = tile % n_blocks;
-            const int ti = find_segment(blk_prefix, nseg, g);
-            const int s = ti < GL ? (ti % G) * Lg + ti / G : ti;
-            const int blk = g - blk_prefix[ti];
+            const int s = find_segment(blk_prefix, nseg, g);
+            const int blk = g - blk_prefix[s];
             const int seg_rows = s_start[s + 1] - s_start[s];
             // This warp's 32 rows start at segment row w_row0; nrows_w of them are in the segment.
             const int w_row0 = blk * kBlockRows + int(crank) * kTileM + quad * 32;
             const int nrows_w = seg_rows - w_row0;
-            // Row 0 of the segment at its destination: the local output, or
-            // in scatter mode the sender's buffer on the rank that sent it.
-            uint16_t* dst0 = dst_base ? reinterpret_cast<uint16_t*>(dst_base[s_expsrc[s] >> 16]) +
-                                            int64_t(s_dst_row[s]) * out_stride
-                                      : out + int64_t(s_start[s]) * out_stride;
-            dst0 += int64_t(w_row0) * out_stride;
+            // Destinations: consecutive rows of the local output, or in
+            // scatter mode each row's own return address (lane r holds row r's).
+            uint16_t* dst0 = dst_base ? nullptr : out + (int64_t(s_start[s]) + w_row0) * out_stride;
+            uint16_t* lane_row = nullptr;
+            if (dst_base && lane < nrows_w) {
+                const int64_t rr = row_ret[int64_t(s_start[s]) + w_row0 + lane];
+                lane_row = reinterpret_cast<uint16_t*>(dst_base[int(rr >> 32)]) + int64_t(uint32_t(rr)) * out_stride;
+            }
             const uint32_t t_row = tmem + uint32_t(buf) * kTileN + (uint32_t(quad * 32) << 16);
             if (EPI == kEpiSwiGLU) {
                 // 32 gate + 32 up columns per TMEM round trip; every second
@@ -498,7 +488,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                         stage_put(stg, lane, ch, make_uint4(o[0], o[1], o[2], o[3]));
                         stage_put(stg, lane, ch + 1, make_uint4(o[4], o[5], o[6], o[7]));
                     }
-                    if (c & 32) stage_flush(stg, lane, dst0, out_stride, nrows_w, n * (kTileN / 2) + c - 32, n_out);
+                    if (c & 32)
+                        stage_flush(stg, lane, dst0, out_stride, nrows_w, n * (kTileN / 2) + c - 32, n_out, lane_row);
                 }
             } else {
                 // 64 columns per TMEM round trip
@@ -517,7 +508,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                         stage_put(stg, lane, 2 * q4, make_uint4(o[0], o[1], o[2], o[3]));
                         stage_put(stg, lane, 2 * q4 + 1, make_uint4(o[4], o[5], o[6], o[7]));
                     }
-                    stage_flush(stg, lane, dst0, out_stride, nrows_w, n * kTileN + c, n_out);
+                    stage_flush(stg, lane, dst0, out_stride, nrows_w, n * kTileN + c, n_out, lane_row);
                 }
             }
             tc_fence_before();
@@ -554,7 +545,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
 template <int CG>
 static size_t ffn_smem_bytes(int nseg) {
     return 1024 + Geo<CG>::kStages * (kABytes + Geo<CG>::kBBytes) + kStageBytes + sizeof(FfnSmem) +
-           size_t(4 * nseg + 2) * 4;
+           size_t(3 * nseg + 2) * 4;
 }
 
 static int sm_count_ffn() {
@@ -580,8 +571,7 @@ static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb_, co
                                const int32_t* seg_expert, int nseg, int rows, int kdim, int b_rows_per_expert,
                                int n_out, int n_blocks, int split, void* out, int64_t out_stride,
                                uint32_t* st, cudaStream_t stream, char* const* dst_base = nullptr,
-                               const int32_t* seg_src = nullptr, const int32_t* seg_dst_row = nullptr,
-                               int seg_groups = 1, int seg_group_len = 0, const int32_t* gather_rows = nullptr,
+                               const int64_t* row_ret = nullptr, const int32_t* gather_rows = nullptr,
                                int gather_limit = 0, const EpSignal* sig = nullptr) {
     EpSignal no_sig{};
     const size_t smem = ffn_smem_bytes<CG>(nseg);
@@ -609,35 +599,30 @@ static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb_, co
     if (max_tiles < groups) groups = int(max_tiles > 0 ? max_tiles : 1);
     cfg.gridDim = dim3(CG * groups);
     return cudaLaunchKernelEx(&cfg, kern, ma, mb_, seg_start, seg_expert, nseg, kdim, b_rows_per_expert, n_out,
-                              n_blocks, split, static_cast<uint16_t*>(out), out_stride, st, dst_base, seg_src,
-                              seg_dst_row, seg_groups, seg_group_len, gather_rows, gather_limit,
-                              sig ? *sig : no_sig);
+                              n_blocks, split, static_cast<uint16_t*>(out), out_stride, st, dst_base, row_ret,
+                              gather_rows, gather_limit, sig ? *sig : no_sig);
 }
 
 template <int DT>
 static cudaError_t launch_ffn(int cg, const CUtensorMap& mx, const CUtensorMap& mwgu, const CUtensorMap& mh,
                               const CUtensorMap& mwd, const int32_t* seg_start, const int32_t* seg_expert, int nseg,
                               int rows, int d, int I, void* h, void* y, uint32_t* st, cudaStream_t s,
-                              char* const* dst_base, const int32_t* seg_src, const int32_t* seg_dst_row,
-                              int seg_groups, int seg_group_len, const int32_t* gather_rows, int gather_T,
-                              const EpSignal* sig) {
+                              char* const* dst_base, const int64_t* row_ret, const int32_t* gather_rows,
+                              int gather_T, const EpSignal* sig) {
     const int nb1 = (I + kTileN / 2 - 1) / (kTileN / 2);
     const int nb2 = (d + kTileN - 1) / kTileN;
     // The gathered form of GEMM 1 runs on single SMs.
     cudaError_t err =
         ((cg & 1) && !gather_rows)
             ? launch_gemm<kEpiSwiGLU, DT, 2>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1, I, h, I,
-                                             st, s, nullptr, nullptr, nullptr, seg_groups, seg_group_len)
+                                             st, s)
             : launch_gemm<kEpiSwiGLU, DT, 1>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1, I, h, I,
-                                             st, s, nullptr, nullptr, nullptr, seg_groups, seg_group_len, gather_rows,
-                                             gather_T);
+                                             st, s, nullptr, nullptr, gather_rows, gather_T);
     if (err != cudaSuccess) return err;
     return (cg & 2) ? launch_gemm<kEpiStore, DT, 2>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0, y, d,
-                                                    st, s, dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len,
-                                                    nullptr, 0, sig)
+                                                    st, s, dst_base, row_ret, nullptr, 0, sig)
                     : launch_gemm<kEpiStore, DT, 1>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0, y, d,
-                                                    st, s, dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len,
-                                                    nullptr, 0, sig);
+                                                    st, s, dst_base, row_ret, nullptr, 0, sig);
 }
 
 int fail(int code, const char* fmt, ...);
@@ -648,9 +633,8 @@ int cuda_fail(cudaError_t err, const char* where);
 namespace moe_b200 {
 int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* seg_expert, int nseg, int rows,
                         int d, int I, int E, const void* w_gate_up, const void* w_down, int dtype, void* h,
-                        void* y, cudaStream_t s, char* const* dst_base, const int32_t* seg_src,
-                        const int32_t* seg_dst_row, int seg_groups, int seg_group_len, const int32_t* gather_rows,
-                        int gather_T, const EpSignal* sig) {
+                        void* y, cudaStream_t s, char* const* dst_base, const int64_t* row_ret,
+                        const int32_t* gather_rows, int gather_T, const EpSignal* sig) {
     if (nseg < 1 || rows < 0 || d < 1 || I < 1 || E < 1)
         return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: need nseg>=1, rows>=0, d>=1, I>=1, E>=1");
     if (nseg > kMaxSegments)
@@ -664,8 +648,8 @@ int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* 
     const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w_gate_up) |
                          reinterpret_cast<uintptr_t>(w_down) | reinterpret_cast<uintptr_t>(h) |
                          reinterpret_cast<uintptr_t>(y);
-    if (dst_base && (!seg_src || !seg_dst_row))
-        return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: scatter mode needs seg_src and seg_dst_row");
+    if (dst_base && !row_ret)
+        return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: scatter mode needs the rows' return addresses");
     if (al % 16 != 0) return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: pointers must be 16-byte aligned");
     if (rows == 0 && !sig) return MOE_B200_OK;
     uint32_t* st = device_status_word();
@@ -685,11 +669,9 @@ int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* 
     const cudaError_t err =
         dtype == MOE_B200_BF16
             ? launch_ffn<MOE_B200_BF16>(cg, mx, mwgu, mh, mwd, seg_start, seg_expert, nseg, rows, d, I, h, y, st, s,
-                                        dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len, gather_rows,
-                                        gather_T, sig)
+                                        dst_base, row_ret, gather_rows, gather_T, sig)
             : launch_ffn<MOE_B200_F16>(cg, mx, mwgu, mh, mwd, seg_start, seg_expert, nseg, rows, d, I, h, y, st, s,
-                                       dst_base, seg_src, seg_dst_row, seg_groups, seg_group_len, gather_rows,
-                                       gather_T, sig);
+                                       dst_base, row_ret, gather_rows, gather_T, sig);
     return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "grouped_swiglu launch");
 }
 }  // namespace moe_b200
@@ -810,8 +792,8 @@ extern "C" int moe_b200_grouped_swiglu(const void* x, const int32_t* seg_start, 
                                        int nseg, int rows, int d, int I, int E, const void* w_gate_up,
                                        const void* w_down, int dtype, void* h, void* y, void* stream) {
     return moe_b200::grouped_swiglu_impl(x, seg_start, seg_expert, nseg, rows, d, I, E, w_gate_up, w_down, dtype,
-                                         h, y, static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr, 1, 0,
-                                         nullptr, 0, nullptr);
+                                         h, y, static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr, 0,
+                                         nullptr);
 }
 
 extern "C" int moe_b200_grouped_swiglu_gather(const void* x_tokens, int T, const int32_t* row_token,
@@ -821,6 +803,6 @@ extern "C" int moe_b200_grouped_swiglu_gather(const void* x_tokens, int T, const
     if (!row_token || T < 1)
         return moe_b200::fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu_gather: need row_token and T >= 1");
     return moe_b200::grouped_swiglu_impl(x_tokens, seg_start, seg_expert, nseg, rows, d, I, E, w_gate_up, w_down,
-                                         dtype, h, y, static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr,
-                                         1, 0, row_token, T, nullptr);
+                                         dtype, h, y, static_cast<cudaStream_t>(stream), nullptr, nullptr, row_token,
+                                         T, nullptr);
 }

@@ -247,9 +247,9 @@ class FusedExpertParallel:
         buf = (ctypes.c_uint8 * (self.N * 64))(*allh.cpu().tolist())
         mb._check(self.L_.moe_b200_ep_connect(self.ctx, buf), "ep_connect")
         self.epoch = 0
-        nseg = self.N * self.L_range + len(rep_ids)
+        nseg = n_local   # one receive segment per local expert (expert-major receive buffer)
         mk = lambda n: torch.empty(n, dtype=torch.int32, device=device)
-        self.seg_start, self.seg_expert, self.seg_src, self.seg_dst_row = mk(nseg + 1), mk(nseg), mk(nseg), mk(nseg)
+        self.seg_start, self.seg_expert = mk(nseg + 1), mk(nseg)
         self.recv_cap = int(self.L_.moe_b200_ep_recv_capacity(self.ctx))
 
     def _s(self, stream):
@@ -289,14 +289,12 @@ class FusedExpertParallel:
     def receive(self, stream=None):
         p = self.mb._ptr
         self.mb._check(self.L_.moe_b200_ep_receive(self.ctx, self.epoch, p(self.seg_start), p(self.seg_expert),
-                                                   p(self.seg_src), p(self.seg_dst_row), self._s(stream)),
-                       "ep_receive")
+                                                   self._s(stream)), "ep_receive")
 
     def return_identity(self, stream=None):
         p = self.mb._ptr
         self.mb._check(self.L_.moe_b200_ep_return_identity(self.ctx, self.epoch, p(self.seg_start),
-                                                           p(self.seg_src), p(self.seg_dst_row), self._s(stream)),
-                       "ep_return_identity")
+                                                           self._s(stream)), "ep_return_identity")
 
     def ffn_return(self, w_gate_up, w_down, h, stream=None):
         """Grouped SwiGLU on the received rows: w_gate_up [n, 2I, d] /
@@ -305,8 +303,8 @@ class FusedExpertParallel:
         p = self.mb._ptr
         I = w_down.shape[2]
         self.mb._check(self.L_.moe_b200_ep_ffn_return(
-            self.ctx, self.epoch, p(self.seg_start), p(self.seg_expert), p(self.seg_src), p(self.seg_dst_row), I,
-            p(w_gate_up), p(w_down), self.mb.dtype_code(self.dtype), p(h), self._s(stream)), "ep_ffn_return")
+            self.ctx, self.epoch, p(self.seg_start), p(self.seg_expert), I, p(w_gate_up), p(w_down),
+            self.mb.dtype_code(self.dtype), p(h), self._s(stream)), "ep_ffn_return")
 
     def combine(self, packed_weights, slot_pos, T, out, stream=None):
         p = self.mb._ptr

@@ -115,11 +115,11 @@ def lib() -> ctypes.CDLL:
     L.moe_b200_ep_dispatch.restype = cint
     L.moe_b200_ep_dispatch.argtypes = [vp, u64, vp, vp, vp, cint, vp, vp, vp, vp, vp, vp, sz, vp]
     L.moe_b200_ep_receive.restype = cint
-    L.moe_b200_ep_receive.argtypes = [vp, u64, vp, vp, vp, vp, vp]
+    L.moe_b200_ep_receive.argtypes = [vp, u64, vp, vp, vp]
     L.moe_b200_ep_return_identity.restype = cint
-    L.moe_b200_ep_return_identity.argtypes = [vp, u64, vp, vp, vp, vp]
+    L.moe_b200_ep_return_identity.argtypes = [vp, u64, vp, vp]
     L.moe_b200_ep_ffn_return.restype = cint
-    L.moe_b200_ep_ffn_return.argtypes = [vp, u64, vp, vp, vp, vp, cint, vp, vp, cint, vp, vp]
+    L.moe_b200_ep_ffn_return.argtypes = [vp, u64, vp, vp, cint, vp, vp, cint, vp, vp]
     L.moe_b200_ep_combine.restype = cint
     L.moe_b200_ep_combine.argtypes = [vp, u64, vp, vp, cint, cint, vp, vp]
     L.moe_b200_ep_step.restype = cint

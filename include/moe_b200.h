@@ -253,8 +253,9 @@ int moe_b200_ep_layout(const int32_t* all_counts, int nranks, int E, int rank,
 /* ------------------------------ fused expert parallel over peer memory ---- */
 
 /* One process per GPU.  A context owns this rank's symmetric region (receive
- * rows for up to nranks*max_tokens*K rows, back rows, counts inbox, epoch
- * flags), which the peers map through CUDA IPC.  Lifecycle:
+ * rows for up to nranks*max_tokens*K rows with each row's return address,
+ * back rows, counts inbox, epoch flags), which the peers map through CUDA
+ * IPC.  Lifecycle:
  *   moe_b200_ep_create -> moe_b200_ep_ipc_handle (64 bytes) -> exchange the
  *   handles between the ranks (any host channel) -> moe_b200_ep_connect with
  *   all nranks handles in rank order -> steps -> barrier -> moe_b200_ep_destroy.
@@ -265,12 +266,15 @@ int moe_b200_ep_layout(const int32_t* all_counts, int nranks, int E, int rank,
  *                                 token row straight into the receive buffer
  *                                 of the rank owning its expert
  *   moe_b200_ep_receive           wait for all senders; segment table of the
- *                                 receive buffer (seg_* arrays of
- *                                 nranks*L' + H (+1) entries: L' = this rank's
+ *                                 receive buffer, which is expert-major: one
+ *                                 segment per local expert holding every
+ *                                 sender's rows (seg_start L'+H+1 entries,
+ *                                 seg_expert L'+H: L' = this rank's
  *                                 non-replicated experts, H = replicated ones)
  *   moe_b200_ep_ffn_return        grouped SwiGLU on the received rows whose
  *                                 down-GEMM stores every row straight into
- *                                 the sender's back buffer
+ *                                 the sender's back buffer, at the return
+ *                                 address the dispatch stored beside it
  *     or moe_b200_ep_return_identity   (identity expert)
  *   moe_b200_ep_combine           wait for all returns; weighted unpermute
  * or all of it with one call, moe_b200_ep_step.
@@ -303,12 +307,10 @@ int moe_b200_ep_dispatch(void* ctx, uint64_t epoch, const void* emb, const int32
                          int32_t* expert_count, int32_t* expert_start, int32_t* slot_pos,
                          void* workspace, size_t workspace_bytes, void* stream);
 int moe_b200_ep_receive(void* ctx, uint64_t epoch, int32_t* seg_start, int32_t* seg_expert,
-                        int32_t* seg_src, int32_t* seg_dst_row, void* stream);
-int moe_b200_ep_return_identity(void* ctx, uint64_t epoch, const int32_t* seg_start,
-                                const int32_t* seg_src, const int32_t* seg_dst_row, void* stream);
+                        void* stream);
+int moe_b200_ep_return_identity(void* ctx, uint64_t epoch, const int32_t* seg_start, void* stream);
 int moe_b200_ep_ffn_return(void* ctx, uint64_t epoch, const int32_t* seg_start,
-                           const int32_t* seg_expert, const int32_t* seg_src,
-                           const int32_t* seg_dst_row, int I, const void* w_gate_up,
+                           const int32_t* seg_expert, int I, const void* w_gate_up,
                            const void* w_down, int dtype, void* h, void* stream);
 int moe_b200_ep_combine(void* ctx, uint64_t epoch, const float* packed_weights,
                         const int32_t* slot_pos, int T, int dtype, void* out, void* stream);
