@@ -28,7 +28,10 @@ static_assert(sizeof(WsHeader) == 256, "header is one 256-byte block");
 
 constexpr int kScanWarps = 8;                    // route/scan CTA: 8 warps
 constexpr int kScanThreads = kScanWarps * 32;
-constexpr int kScanChunks = 8;                   // 32-slot chunks per warp
+#ifndef MOE_B200_SCAN_CHUNKS
+#define MOE_B200_SCAN_CHUNKS 8
+#endif
+constexpr int kScanChunks = MOE_B200_SCAN_CHUNKS;  // 32-slot chunks per warp
 constexpr int kTileSlots = kScanThreads * kScanChunks;  // 2048 slots per tile
 
 struct PackPlan {

@@ -63,6 +63,8 @@ def parse(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-layer", action="store_true",
                     help="pack configs: skip the c5 layer measurement that the line carries as `layer`")
+    ap.add_argument("--no-c3", action="store_true",
+                    help="N=1 default: skip the c3 (prefill-scale packing) measurement the line carries as `c3`")
     ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                     help="N>1 expert placement: popularity dealt round-robin over ranks (default) or the "
                          "reference's contiguous ranges")
@@ -574,7 +576,7 @@ def expert_weights(labels, orig_of, I, d, tdtype, dev):
     return wgu, wdn
 
 
-def run_config(args, job, cfg_name, clock, headline):
+def run_config(args, job, cfg_name, clock, headline, e2e=True):
     """Measures one config at the job's GPU count.  Returns a dict of results
     (rank 0's view; every rank takes the same collective steps)."""
     import torch
@@ -822,7 +824,7 @@ def run_config(args, job, cfg_name, clock, headline):
     if headline and world == 1 and not layer and not args.no_router:
         res["router"] = router_leg(mb, c, emb, stream, dev, flusher, steps, warm)
 
-    if not args.no_e2e:
+    if e2e and not args.no_e2e:
         res["e2e"] = e2e_leg(job, c, emb, asgn_np, wts_np, enqueue, stream, steps, warm, layer)
     if fep is not None:
         fep.close()
@@ -987,6 +989,10 @@ def gpu_arm(args):
     if not res["layer"] and not args.no_layer:
         torch.cuda.empty_cache()
         lay = run_config(args, job, "c5", NullClock(), headline=False)
+    big = None
+    if args.config == "c2" and world == 1 and not args.no_c3:
+        torch.cuda.empty_cache()
+        big = run_config(args, job, "c3", NullClock(), headline=False, e2e=False)
 
     if rank == 0:
         c = res["c"]
@@ -1097,6 +1103,16 @@ def gpu_arm(args):
             line["router"] = res["router"]
         if lay is not None:
             line["layer"] = layer_summary(lay, world)
+        if big is not None:
+            b3p, b3u = algorithmic_bytes(big["c"])
+            ms3 = big["ms"]
+            line["c3"] = {
+                "metric": METRIC, "unit": UNIT, "value": big["T"] * big["steps"] / (big["total_ms"] / 1e3),
+                "ms_per_step": ms3, "workload": config_json(big["c"], 1, L2_NOTE)["workload"],
+                "hbm_gbs": (b3p + b3u) / (ms3 / 1e3) / 1e9, "frac": (b3p + b3u) / (ms3 / 1e3) / 1e9 / peak_hbm,
+                "stages_ms": {"pack": big["stages"]["pack"], "unpermute": big["stages"]["unpermute"]},
+                "algorithmic_bytes_per_step": b3p + b3u, "parity": big["parity"],
+                "note": "prefill-scale packing (BASELINE config 3), same step and timing as the headline"}
         if world == 1 and not args.no_cpu_baseline and not layer:
             cv, per, kind, n = run_cpu(c, 1, c["T"], 5, 1, min_seconds=10.0)
             line["cpu_baseline"] = {

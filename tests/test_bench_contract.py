@@ -73,3 +73,22 @@ def test_clock_summary_names_reasons_from_nvml_bits():
                "0, 1950, 1965, 710.0, 0x0, Not Active, Not Active, Not Active, Not Active"]
     s = c.summary()
     assert s["sm_mhz"] == 1957.5 and s["sm_max_mhz"] == 1965.0 and s["reasons"] == ["sw_power_cap"]
+
+
+def test_exchange_byte_model_and_step_stats():
+    """bench.exchange_bytes: rows a rank sends to / receives from other ranks
+    (non-replicated experts owned elsewhere), the survey's EP byte model, on
+    a hand-checked 2-rank case; bench.stats_ms on a known list."""
+    sys.path.insert(0, ROOT)
+    import numpy as np
+    import bench
+    # E = 4 experts, ranks own [0, 2) and [2, 4); expert 1 replicated
+    counts = np.array([[5, 7, 2, 1],     # rank 0's rows per expert
+                       [3, 4, 6, 8]])    # rank 1's
+    res = {"counts": counts, "bounds": [0, 2, 4], "replicated": [1], "c": {"E": 4, "d": 8}}
+    send, recv = bench.exchange_bytes(res, 2)
+    row = 8 * 2
+    assert send == [(2 + 1) * row, 3 * row]      # rank 0 -> experts 2, 3; rank 1 -> expert 0 (1 is local)
+    assert recv == [3 * row, (2 + 1) * row]
+    s = bench.stats_ms([5.0, 1.0, 3.0, 2.0, 4.0])
+    assert s["median"] == 3.0 and s["max"] == 5.0 and s["min"] == 1.0 and s["p90"] == 5.0
