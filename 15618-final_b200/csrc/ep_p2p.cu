@@ -149,7 +149,8 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
     // receive row of packed position p there = s_dst[e] + p
     extern __shared__ int64_t s_dst[];                          // [E]
     int32_t* s_owner = reinterpret_cast<int32_t*>(s_dst + g.E);  // [E]
-    int32_t* s_inbox = s_owner + g.E;                            // [N][E] when inbox_smem
+    int32_t* s_start = s_owner + g.E;                            // [E] this rank's packed expert starts
+    int32_t* s_inbox = s_start + g.E;                            // [N][E] when inbox_smem
     const int K = g.K, nvec = g.d / 8;
     if (threadIdx.x == 0) s_fail = 0;
     __syncthreads();
@@ -159,13 +160,15 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
     wait_flags(reinterpret_cast<const uint64_t*>(mine + g.off_cflag), g.nranks, epoch, g.timeout_ns, dev_status,
                &s_fail);
     const int32_t* inbox = reinterpret_cast<const int32_t*>(mine + g.off_inbox);
+    // one coalesced pass over every rank's counts and this rank's starts, so
+    // the serial offset loops below read shared memory instead of chains of
+    // global loads while the rest of the CTA waits at the barrier
+    for (int e = threadIdx.x; e < g.E; e += blockDim.x) s_start[e] = expert_start[e];
     if (inbox_smem) {
-        // one coalesced pass over every rank's counts, so the serial prefix
-        // loops below read shared memory instead of chains of global loads
         for (int i = threadIdx.x; i < g.nranks * g.E; i += blockDim.x) s_inbox[i] = inbox[i];
-        __syncthreads();
         inbox = s_inbox;
     }
+    __syncthreads();
     const int32_t* own = inbox + size_t(g.rank) * g.E;  // this rank's counts
     // Receiver r (thread r): its non-replicated experts in ascending order,
     // each holding every sender's rows in sender order; this sender's rows of
@@ -183,7 +186,7 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
                 before += s < g.rank ? c : 0;
             }
             s_owner[e] = r;
-            s_dst[e] = base + before - expert_start[e];
+            s_dst[e] = base + before - s_start[e];
             base += col;
         }
         if (r == g.rank) s_hot_base = base;  // this rank's replicated block follows
@@ -194,7 +197,7 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
         for (int e = 0; e < g.E; ++e) {
             if (!ep_is_hot(g, e)) continue;
             s_owner[e] = g.rank;
-            s_dst[e] = base - expert_start[e];
+            s_dst[e] = base - s_start[e];
             base += own[e];
         }
     }
@@ -213,7 +216,7 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
             int32_t p = -1;
             if (r >= 0) {
                 const int e = __ldg(asgn + sidx);
-                p = expert_start[e] + r;
+                p = s_start[e] + r;
                 perm[p] = int32_t(t);
                 if (packed_w) packed_w[p] = __ldg(wts + sidx);
                 const int owner = s_owner[e];
@@ -332,12 +335,45 @@ ep_receive_kernel(EpGeom g, char* const* __restrict__ peer, uint64_t epoch, int3
 constexpr int kReturnVPL = 8;  // 16-byte vectors per lane per pass: 4 KB rows in one pass
 constexpr int64_t kRowStride = 2147483647;  // 2^31 - 1, prime
 
+// seg_start == nullptr (the one-call step): no receive kernel ran before
+// this one, so every CTA waits (bounded) for the senders' data flags itself
+// and counts the received rows from the counts inbox.
 __global__ void __launch_bounds__(256)
-ep_return_identity_kernel(EpGeom g, char* const* __restrict__ back, const uint4* __restrict__ recv,
-                          const int64_t* __restrict__ ret, const int32_t* __restrict__ seg_start, int nseg,
-                          EpSignal sig) {
+ep_return_identity_kernel(EpGeom g, char* const* __restrict__ peer, char* const* __restrict__ back,
+                          const uint4* __restrict__ recv, const int64_t* __restrict__ ret,
+                          const int32_t* __restrict__ seg_start, int nseg, EpSignal sig,
+                          uint32_t* __restrict__ dev_status) {
+    __shared__ int s_fail;
+    __shared__ unsigned long long s_total;
+    if (threadIdx.x == 0) {
+        s_fail = 0;
+        s_total = 0;
+    }
+    __syncthreads();
     pdl_wait_primary();
-    const int64_t total = seg_start[nseg];
+    int64_t total;
+    if (seg_start) {
+        total = seg_start[nseg];
+    } else {
+        const char* mine = peer[g.rank];
+        wait_flags(reinterpret_cast<const uint64_t*>(mine + g.off_dflag), g.nranks, sig.epoch, g.timeout_ns,
+                   dev_status, &s_fail);
+        // rows here: every sender's rows of the range's non-replicated
+        // experts + this rank's own rows of the replicated ones
+        const int32_t* inbox = reinterpret_cast<const int32_t*>(mine + g.off_inbox);
+        unsigned long long part = 0;
+        for (int i = threadIdx.x; i < g.nranks * g.E; i += blockDim.x) {
+            const int s = i / g.E, e = i % g.E;
+            const bool hot = ep_is_hot(g, e);
+            if ((!hot && e >= g.first[g.rank] && e < g.first[g.rank + 1]) || (hot && s == g.rank))
+                part += unsigned(inbox[i]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+        if ((threadIdx.x & 31) == 0) atomicAdd(&s_total, part);
+        __syncthreads();
+        total = int64_t(s_total);
+    }
     const int nvec = g.d / 8;
     const int lane = threadIdx.x & 31;
     const int64_t gw = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -361,10 +397,11 @@ ep_return_identity_kernel(EpGeom g, char* const* __restrict__ back, const uint4*
             }
         }
     }
-    // the last CTA to finish raises the back flags of every sender
+    // the last CTA to finish raises the back flags of every sender (not
+    // when a CTA gave up waiting for the rows: then the senders time out too)
     __threadfence_system();
     __syncthreads();
-    if (threadIdx.x == 0) ep_signal_done(sig, false);
+    if (threadIdx.x == 0) ep_signal_done(sig, s_fail != 0);
 }
 
 // ------------------------------------------------------------------ host ----
@@ -575,7 +612,7 @@ static int ep_enqueue_dispatch(EpContext* ctx, uint64_t epoch, const void* emb, 
         if (grid > want) grid = want;
         // the counts inbox goes to shared memory when it is small (N*E <= 4096)
         const int inbox_smem = int64_t(g.nranks) * g.E <= kInboxSmemMax ? 1 : 0;
-        const size_t smem = size_t(g.E) * 12 + (inbox_smem ? size_t(g.nranks) * g.E * 4 : 0);
+        const size_t smem = size_t(g.E) * 16 + (inbox_smem ? size_t(g.nranks) * g.E * 4 : 0);
         cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(256), smem, s);
         cudaLaunchAttribute attr = pdl_attr();
         cfg.attrs = &attr;
@@ -610,17 +647,22 @@ static EpSignal back_signal(EpContext* ctx, int which, uint64_t epoch) {
                     reinterpret_cast<uint32_t*>(ctx->region + g.off_count) + 2 * which, g.rank, g.nranks, epoch};
 }
 
+// seg_start == nullptr: the return kernel waits for the senders itself (no
+// receive kernel before it).
 static int ep_enqueue_return_identity(EpContext* ctx, uint64_t epoch, const int32_t* seg_start, cudaStream_t s) {
     const EpGeom& g = ctx->g;
     const int nseg = g.lrange + g.nhot;
+    uint32_t* st = device_status_word();
+    if (!st) return fail(MOE_B200_ERR_CUDA, "ep_return_identity: device status word unavailable");
     cudaLaunchConfig_t cfg = pdl_config(dim3(sm_count_ep() * 4), dim3(256), 0, s);
     cudaLaunchAttribute attr = pdl_attr();
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
-    cudaError_t err = cudaLaunchKernelEx(&cfg, ep_return_identity_kernel, g, static_cast<char* const*>(ctx->back_dev),
+    cudaError_t err = cudaLaunchKernelEx(&cfg, ep_return_identity_kernel, g, static_cast<char* const*>(ctx->peer_dev),
+                                         static_cast<char* const*>(ctx->back_dev),
                                          reinterpret_cast<const uint4*>(ctx->region + g.off_recv),
                                          reinterpret_cast<const int64_t*>(ctx->region + g.off_ret), seg_start, nseg,
-                                         back_signal(ctx, 0, epoch));
+                                         back_signal(ctx, 0, epoch), st);
     return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "ep_return_identity launch");
 }
 
@@ -718,9 +760,11 @@ int moe_b200_ep_step(void* c, const void* emb, const int32_t* asgn, const float*
     int32_t* seg_expert = seg_start + (g.E + 1);   // [E]
     int st = ep_enqueue_dispatch(ctx, epoch, emb, asgn, wts, T, packed_weights, perm, expert_count, expert_start,
                                  slot_pos, workspace, workspace_bytes, s);
-    if (st == MOE_B200_OK) st = ep_enqueue_receive(ctx, epoch, seg_start, seg_expert, s);
+    // identity: the return kernel waits for the senders itself (four launches
+    // per step); the FFN needs the receive kernel's segment table
+    if (st == MOE_B200_OK && !identity) st = ep_enqueue_receive(ctx, epoch, seg_start, seg_expert, s);
     if (st == MOE_B200_OK)
-        st = identity ? ep_enqueue_return_identity(ctx, epoch, seg_start, s)
+        st = identity ? ep_enqueue_return_identity(ctx, epoch, nullptr, s)
                       : ep_enqueue_ffn_return(ctx, epoch, seg_start, seg_expert, I, w_gate_up, w_down, dtype, h, s);
     if (st == MOE_B200_OK) st = ep_enqueue_combine(ctx, epoch, packed_weights, slot_pos, T, dtype, out, s);
     return st;

@@ -12,7 +12,7 @@ One step = one pass of the hot path over one batch:
           selects the AllToAllv variant), applies the identity expert, returns
           the rows the same way and unpermutes: weak scaling, value = all
           ranks' tokens / max-rank time.  The fused step is ONE library call
-          per rank (moe_b200_ep_step, five kernels).
+          per rank (moe_b200_ep_step, four kernels for the identity expert).
 
 Prints ONE JSON line on rank 0.  `value` is device-timed (CUDA events on the
 launching stream, created before the loop; inputs resident in HBM; L2 flushed
@@ -914,9 +914,10 @@ def e2e_leg(job, c, emb_dev, asgn_np, wts_np, enqueue, stream, steps, warm, laye
 def kernels_of(res, world):
     layer, fused, gather = res["layer"], res["fused"], res["gather"]
     if fused:
-        return ["route_scan_kernel (+ count publish)", "ep_pack_dispatch_kernel", "ep_receive_kernel"] + \
-            (["grouped_gemm_kernel<SwiGLU>", "grouped_gemm_kernel<store, peer scatter, + back-flag signal>"]
-             if layer else ["ep_return_identity_kernel (+ back-flag signal)"]) + \
+        expert = (["ep_receive_kernel", "grouped_gemm_kernel<SwiGLU>",
+                   "grouped_gemm_kernel<store, peer scatter, + back-flag signal>"] if layer
+                  else ["ep_return_identity_kernel (+ data-flag wait, back-flag signal)"])
+        return ["route_scan_kernel (+ count publish)", "ep_pack_dispatch_kernel"] + expert + \
             ["unpermute_bulk_kernel (+ back-flag wait)"]
     if gather:
         return ["route_scan_kernel", "pack_index_kernel", "grouped_gemm_kernel<SwiGLU, gathered rows>",

@@ -316,9 +316,10 @@ int moe_b200_ep_combine(void* ctx, uint64_t epoch, const float* packed_weights,
                         const int32_t* slot_pos, int T, int dtype, void* out, void* stream);
 
 /* One whole step in one call: dispatch -> receive -> expert -> combine with
- * the next epoch (moe_b200_ep_epoch(ctx) + 1), five kernel launches for the
- * identity expert (w_gate_up = w_down = NULL; I and h unused) and six for the
- * grouped SwiGLU (w_gate_up / w_down / h as moe_b200_ep_ffn_return).  The
+ * the next epoch (moe_b200_ep_epoch(ctx) + 1), four kernel launches for the
+ * identity expert (w_gate_up = w_down = NULL; I and h unused; its return
+ * kernel waits for the senders itself) and six for the grouped SwiGLU
+ * (w_gate_up / w_down / h as moe_b200_ep_ffn_return).  The
  * segment table lives in the context.  Arguments otherwise as the stage
  * calls; out [T, d] receives the combined rows.  Replaces one round of
  * apps/bench_prefill.cu:768-906 (count all-gather, host offsets, dispatch
