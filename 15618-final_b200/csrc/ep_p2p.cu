@@ -65,7 +65,8 @@ cudaError_t launch_unpermute(const void* y, const float* packed_w, const int32_t
 int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* seg_expert, int nseg, int rows,
                         int d, int I, int E, const void* w_gate_up, const void* w_down, int dtype, void* h,
                         void* y, cudaStream_t s, char* const* dst_base, const int64_t* row_ret,
-                        const int32_t* gather_rows, int gather_T, const EpSignal* sig);
+                        const int32_t* gather_rows, int gather_T, const EpSignal* sig, const EpWait* rows_wait,
+                        int wait_seg0);
 
 constexpr int kEpMaxRanks = 64;
 
@@ -144,7 +145,6 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
                         uint64_t* __restrict__ status, size_t status_words, uint64_t epoch,
                         uint32_t* __restrict__ dev_status, int inbox_smem) {
     __shared__ int s_fail;
-    __shared__ int64_t s_hot_base;
     // per expert e: the rank whose receive buffer takes its rows, and the
     // receive row of packed position p there = s_dst[e] + p
     extern __shared__ int64_t s_dst[];                          // [E]
@@ -170,13 +170,17 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
     }
     __syncthreads();
     const int32_t* own = inbox + size_t(g.rank) * g.E;  // this rank's counts
-    // Receiver r (thread r): its non-replicated experts in ascending order,
-    // each holding every sender's rows in sender order; this sender's rows of
-    // expert e start after all senders' rows of r's earlier experts and the
-    // rows of senders < rank of expert e.
+    // Receiver r (thread r): its own rows of the replicated experts first
+    // (written by its own dispatch, so its gate/up GEMM can start on them
+    // before the other senders' rows land), then its non-replicated experts
+    // in ascending order, each holding every sender's rows in sender order;
+    // this sender's rows of expert e start after all senders' rows of r's
+    // earlier experts and the rows of senders < rank of expert e.
     if (threadIdx.x < g.nranks) {
         const int r = threadIdx.x;
         int64_t base = 0;
+        for (int e = 0; g.nhot > 0 && e < g.E; ++e)
+            if (ep_is_hot(g, e)) base += inbox[r * g.E + e];
         for (int e = g.first[r]; e < g.first[r + 1]; ++e) {
             if (ep_is_hot(g, e)) continue;
             int64_t before = 0, col = 0;
@@ -189,11 +193,10 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
             s_dst[e] = base + before - s_start[e];
             base += col;
         }
-        if (r == g.rank) s_hot_base = base;  // this rank's replicated block follows
-    }
-    __syncthreads();
-    if (threadIdx.x == 0 && g.nhot > 0) {
-        int64_t base = s_hot_base;
+    } else if (threadIdx.x == g.nranks && g.nhot > 0) {
+        // this rank's rows of the replicated experts: the head of its own
+        // receive buffer
+        int64_t base = 0;
         for (int e = 0; e < g.E; ++e) {
             if (!ep_is_hot(g, e)) continue;
             s_owner[e] = g.rank;
@@ -255,10 +258,12 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
         ep_signal_done(EpSignal{peer, g.off_dflag, hdr->pad, g.rank, g.nranks, epoch}, s_fail != 0);
 }
 
-// Receiver: wait for every sender's rows, then the segment table of the
-// receive buffer: one segment per local expert (the range's non-replicated
-// experts with every sender's rows, then the own rows of the replicated
-// experts), seg_expert = the local expert index.
+// Receiver: wait for every sender's counts (not its rows), then the segment
+// table of the receive buffer: one segment per local expert, the own rows of
+// the replicated experts first, then the range's non-replicated experts with
+// every sender's rows; seg_expert = the local expert index (local experts are
+// numbered non-replicated first, replicated last).  The kernels that read
+// the rows wait for the senders' data flags themselves.
 __global__ void __launch_bounds__(256)
 ep_receive_kernel(EpGeom g, char* const* __restrict__ peer, uint64_t epoch, int32_t* __restrict__ seg_start,
                   int32_t* __restrict__ seg_expert, uint32_t* __restrict__ dev_status, int inbox_smem) {
@@ -272,37 +277,38 @@ ep_receive_kernel(EpGeom g, char* const* __restrict__ peer, uint64_t epoch, int3
     }
     __syncthreads();
     const char* mine = peer[g.rank];
-    wait_flags(reinterpret_cast<const uint64_t*>(mine + g.off_dflag), g.nranks, epoch, g.timeout_ns, dev_status,
+    wait_flags(reinterpret_cast<const uint64_t*>(mine + g.off_cflag), g.nranks, epoch, g.timeout_ns, dev_status,
                &s_fail);
     const int32_t* inbox = reinterpret_cast<const int32_t*>(mine + g.off_inbox);
     if (inbox_smem) {
         for (int i = threadIdx.x; i < g.nranks * g.E; i += blockDim.x) s_inbox[i] = inbox[i];
         inbox = s_inbox;   // published by the __syncthreads below
     }
-    // local experts: [non-replicated experts of the range] + [replicated]
+    // segments in buffer order: [replicated] + [non-replicated of the range]
     __shared__ int16_t s_local[kEpMaxExperts];
     if (threadIdx.x == 0) {
         int n = 0;
-        for (int e = g.first[g.rank]; e < g.first[g.rank + 1]; ++e)
-            if (!ep_is_hot(g, e)) s_local[n++] = int16_t(e);
         for (int e = 0; e < g.E; ++e)
             if (ep_is_hot(g, e)) s_local[n++] = int16_t(e);
+        for (int e = g.first[g.rank]; e < g.first[g.rank + 1]; ++e)
+            if (!ep_is_hot(g, e)) s_local[n++] = int16_t(e);
     }
     __syncthreads();
-    const int L = g.lrange;
-    const int nseg = L + g.nhot;
+    const int L = g.lrange, H = g.nhot;
+    const int nseg = L + H;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     for (int base = 0; base < nseg; base += blockDim.x) {
         const int j = base + tid;
         int32_t v = 0;
         if (j < nseg) {
             const int e = s_local[j];
-            if (j < L) {
-                for (int s = 0; s < g.nranks; ++s) v += inbox[s * g.E + e];
-            } else {
+            if (j < H) {
                 v = inbox[g.rank * g.E + e];
+                seg_expert[j] = L + j;
+            } else {
+                for (int s = 0; s < g.nranks; ++s) v += inbox[s * g.E + e];
+                seg_expert[j] = j - H;
             }
-            seg_expert[j] = j;
         }
         int32_t incl = v;
 #pragma unroll
@@ -335,9 +341,9 @@ ep_receive_kernel(EpGeom g, char* const* __restrict__ peer, uint64_t epoch, int3
 constexpr int kReturnVPL = 8;  // 16-byte vectors per lane per pass: 4 KB rows in one pass
 constexpr int64_t kRowStride = 2147483647;  // 2^31 - 1, prime
 
-// seg_start == nullptr (the one-call step): no receive kernel ran before
-// this one, so every CTA waits (bounded) for the senders' data flags itself
-// and counts the received rows from the counts inbox.
+// Every CTA waits (bounded) for the senders' data flags.  seg_start ==
+// nullptr (the one-call step): no receive kernel ran before this one, so the
+// received rows are counted from the counts inbox.
 __global__ void __launch_bounds__(256)
 ep_return_identity_kernel(EpGeom g, char* const* __restrict__ peer, char* const* __restrict__ back,
                           const uint4* __restrict__ recv, const int64_t* __restrict__ ret,
@@ -351,13 +357,13 @@ ep_return_identity_kernel(EpGeom g, char* const* __restrict__ peer, char* const*
     }
     __syncthreads();
     pdl_wait_primary();
+    const char* mine = peer[g.rank];
+    wait_flags(reinterpret_cast<const uint64_t*>(mine + g.off_dflag), g.nranks, sig.epoch, g.timeout_ns, dev_status,
+               &s_fail);
     int64_t total;
     if (seg_start) {
         total = seg_start[nseg];
     } else {
-        const char* mine = peer[g.rank];
-        wait_flags(reinterpret_cast<const uint64_t*>(mine + g.off_dflag), g.nranks, sig.epoch, g.timeout_ns,
-                   dev_status, &s_fail);
         // rows here: every sender's rows of the range's non-replicated
         // experts + this rank's own rows of the replicated ones
         const int32_t* inbox = reinterpret_cast<const int32_t*>(mine + g.off_inbox);
@@ -670,16 +676,21 @@ static int ep_enqueue_ffn_return(EpContext* ctx, uint64_t epoch, const int32_t* 
                                  const int32_t* seg_expert, int I, const void* w_gate_up, const void* w_down,
                                  int dtype, void* h, cudaStream_t s) {
     const EpGeom& g = ctx->g;
-    // GEMM 2's epilogue stores every finished row straight into the back
-    // buffer of the rank that sent it, at the return address stored beside
-    // the row (scatter mode); its last CTA raises the back flags.  One
-    // segment per local expert: the range's non-replicated ones, then the
-    // replicated ones.
+    // One segment per local expert: the replicated ones first (this rank's
+    // own rows, in place since its dispatch finished), then the range's
+    // non-replicated ones.  GEMM 1 starts on the replicated segments and
+    // its producers wait for every sender's data flag before the first
+    // load of the others.  GEMM 2's epilogue stores every finished row
+    // straight into the back buffer of the rank that sent it, at the return
+    // address stored beside the row (scatter mode); its last CTA raises the
+    // back flags.
     const EpSignal sig = back_signal(ctx, 1, epoch);
+    const EpWait rows{reinterpret_cast<const uint64_t*>(ctx->region + g.off_dflag), g.nranks, epoch, g.timeout_ns};
     return grouped_swiglu_impl(ctx->region + g.off_recv, seg_start, seg_expert, g.lrange + g.nhot,
                                int(g.recv_cap), g.d, I, g.lrange + g.nhot, w_gate_up, w_down, dtype, h,
                                ctx->region + g.off_recv, s, ctx->back_dev,
-                               reinterpret_cast<const int64_t*>(ctx->region + g.off_ret), nullptr, 0, &sig);
+                               reinterpret_cast<const int64_t*>(ctx->region + g.off_ret), nullptr, 0, &sig, &rows,
+                               g.nhot);
 }
 
 static int ep_enqueue_combine(EpContext* ctx, uint64_t epoch, const float* packed_weights, const int32_t* slot_pos,

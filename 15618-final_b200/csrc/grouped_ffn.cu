@@ -186,6 +186,28 @@ __device__ __forceinline__ void stage_flush(const unsigned char* stg, int lane, 
     __syncwarp();
 }
 
+// Rows that other ranks store into this GPU's memory (the expert-parallel
+// receive buffer): before the first TMA load of a segment >= wait_seg0, the
+// producer thread waits (bounded by one deadline) until every sender's data
+// flag reached the epoch, then orders its TMA reads after that acquire.  On
+// a timeout it records MOE_B200_DEV_WAIT_TIMEOUT and goes on.
+__device__ __forceinline__ void wait_rows_once(const EpWait& w, bool& ready, uint32_t* dev_status) {
+    if (ready) return;
+    ready = true;
+    const uint64_t t0 = globaltimer_ns();
+    for (int i = 0; i < w.n; ++i) {
+        while (ld_acquire_sys(w.flags + i) < w.epoch) {
+            if (globaltimer_ns() - t0 > w.timeout_ns) {
+                atomicOr(dev_status, MOE_B200_DEV_WAIT_TIMEOUT);
+                i = w.n;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    fence_proxy_async_global();
+}
+
 // Maps a linear 128-row block index to (segment, block within segment).
 __device__ __forceinline__ int find_segment(const int32_t* blk_prefix, int nseg, int g) {
     int lo = 0, hi = nseg - 1;
@@ -208,7 +230,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                     int gate_up_split, uint16_t* __restrict__ out, int64_t out_stride,
                     uint32_t* __restrict__ dev_status, char* const* __restrict__ dst_base,
                     const int64_t* __restrict__ row_ret, const int32_t* __restrict__ gather_rows,
-                    int gather_limit, EpSignal sig) {
+                    int gather_limit, EpSignal sig, EpWait rows_wait, int wait_seg0) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte aligned stage buffers (SW128 atoms), control block after them.
     unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -313,11 +335,13 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         // box of 64 columns; the 4 rows land as 512 contiguous bytes of the
         // 128-byte-swizzled tile), lane 0 arms the barrier and loads B.
         uint32_t it = 0;
+        bool rows_ready = rows_wait.flags == nullptr;
         const int total_rows = s_start[nseg];
         for (int tile = tile0; tile < total_tiles && !*abort_flag; tile += tile_step) {
             const int g = tile / n_blocks, n = tile % n_blocks;
             const int s = find_segment(blk_prefix, nseg, g);
             const int e = s_exp[s];
+            if (s >= wait_seg0) wait_rows_once(rows_wait, rows_ready, dev_status);  // every lane issues loads
             const int row0 = s_start[s] + (g - blk_prefix[s]) * kBlockRows;
             int r4[4];
 #pragma unroll
@@ -354,10 +378,12 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             uint32_t it = 0;
+            bool rows_ready = rows_wait.flags == nullptr;
             for (int tile = tile0; tile < total_tiles && !*abort_flag; tile += tile_step) {
                 const int g = tile / n_blocks, n = tile % n_blocks;
                 const int s = find_segment(blk_prefix, nseg, g);
                 const int e = s_exp[s];
+                if (s >= wait_seg0) wait_rows_once(rows_wait, rows_ready, dev_status);
                 const int row0 = s_start[s] + (g - blk_prefix[s]) * kBlockRows + int(crank) * kTileM;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const int st = int(it % kStages);
@@ -572,8 +598,10 @@ static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb_, co
                                int n_out, int n_blocks, int split, void* out, int64_t out_stride,
                                uint32_t* st, cudaStream_t stream, char* const* dst_base = nullptr,
                                const int64_t* row_ret = nullptr, const int32_t* gather_rows = nullptr,
-                               int gather_limit = 0, const EpSignal* sig = nullptr) {
+                               int gather_limit = 0, const EpSignal* sig = nullptr,
+                               const EpWait* rows_wait = nullptr, int wait_seg0 = 0) {
     EpSignal no_sig{};
+    EpWait no_wait{};
     const size_t smem = ffn_smem_bytes<CG>(nseg);
     auto kern = grouped_gemm_kernel<EPI, DT, CG>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -600,7 +628,8 @@ static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb_, co
     cfg.gridDim = dim3(CG * groups);
     return cudaLaunchKernelEx(&cfg, kern, ma, mb_, seg_start, seg_expert, nseg, kdim, b_rows_per_expert, n_out,
                               n_blocks, split, static_cast<uint16_t*>(out), out_stride, st, dst_base, row_ret,
-                              gather_rows, gather_limit, sig ? *sig : no_sig);
+                              gather_rows, gather_limit, sig ? *sig : no_sig, rows_wait ? *rows_wait : no_wait,
+                              wait_seg0);
 }
 
 template <int DT>
@@ -608,16 +637,17 @@ static cudaError_t launch_ffn(int cg, const CUtensorMap& mx, const CUtensorMap& 
                               const CUtensorMap& mwd, const int32_t* seg_start, const int32_t* seg_expert, int nseg,
                               int rows, int d, int I, void* h, void* y, uint32_t* st, cudaStream_t s,
                               char* const* dst_base, const int64_t* row_ret, const int32_t* gather_rows,
-                              int gather_T, const EpSignal* sig) {
+                              int gather_T, const EpSignal* sig, const EpWait* rows_wait, int wait_seg0) {
     const int nb1 = (I + kTileN / 2 - 1) / (kTileN / 2);
     const int nb2 = (d + kTileN - 1) / kTileN;
     // The gathered form of GEMM 1 runs on single SMs.
     cudaError_t err =
         ((cg & 1) && !gather_rows)
             ? launch_gemm<kEpiSwiGLU, DT, 2>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1, I, h, I,
-                                             st, s)
+                                             st, s, nullptr, nullptr, nullptr, 0, nullptr, rows_wait, wait_seg0)
             : launch_gemm<kEpiSwiGLU, DT, 1>(mx, mwgu, seg_start, seg_expert, nseg, rows, d, 2 * I, I, nb1, I, h, I,
-                                             st, s, nullptr, nullptr, gather_rows, gather_T);
+                                             st, s, nullptr, nullptr, gather_rows, gather_T, nullptr, rows_wait,
+                                             wait_seg0);
     if (err != cudaSuccess) return err;
     return (cg & 2) ? launch_gemm<kEpiStore, DT, 2>(mh, mwd, seg_start, seg_expert, nseg, rows, I, d, d, nb2, 0, y, d,
                                                     st, s, dst_base, row_ret, nullptr, 0, sig)
@@ -634,7 +664,8 @@ namespace moe_b200 {
 int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* seg_expert, int nseg, int rows,
                         int d, int I, int E, const void* w_gate_up, const void* w_down, int dtype, void* h,
                         void* y, cudaStream_t s, char* const* dst_base, const int64_t* row_ret,
-                        const int32_t* gather_rows, int gather_T, const EpSignal* sig) {
+                        const int32_t* gather_rows, int gather_T, const EpSignal* sig, const EpWait* rows_wait,
+                        int wait_seg0) {
     if (nseg < 1 || rows < 0 || d < 1 || I < 1 || E < 1)
         return fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu: need nseg>=1, rows>=0, d>=1, I>=1, E>=1");
     if (nseg > kMaxSegments)
@@ -669,9 +700,9 @@ int grouped_swiglu_impl(const void* x, const int32_t* seg_start, const int32_t* 
     const cudaError_t err =
         dtype == MOE_B200_BF16
             ? launch_ffn<MOE_B200_BF16>(cg, mx, mwgu, mh, mwd, seg_start, seg_expert, nseg, rows, d, I, h, y, st, s,
-                                        dst_base, row_ret, gather_rows, gather_T, sig)
+                                        dst_base, row_ret, gather_rows, gather_T, sig, rows_wait, wait_seg0)
             : launch_ffn<MOE_B200_F16>(cg, mx, mwgu, mh, mwd, seg_start, seg_expert, nseg, rows, d, I, h, y, st, s,
-                                       dst_base, row_ret, gather_rows, gather_T, sig);
+                                       dst_base, row_ret, gather_rows, gather_T, sig, rows_wait, wait_seg0);
     return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "grouped_swiglu launch");
 }
 }  // namespace moe_b200
@@ -793,7 +824,7 @@ extern "C" int moe_b200_grouped_swiglu(const void* x, const int32_t* seg_start, 
                                        const void* w_down, int dtype, void* h, void* y, void* stream) {
     return moe_b200::grouped_swiglu_impl(x, seg_start, seg_expert, nseg, rows, d, I, E, w_gate_up, w_down, dtype,
                                          h, y, static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr, 0,
-                                         nullptr);
+                                         nullptr, nullptr, 0);
 }
 
 extern "C" int moe_b200_grouped_swiglu_gather(const void* x_tokens, int T, const int32_t* row_token,
@@ -804,5 +835,5 @@ extern "C" int moe_b200_grouped_swiglu_gather(const void* x_tokens, int T, const
         return moe_b200::fail(MOE_B200_ERR_INVALID_ARG, "grouped_swiglu_gather: need row_token and T >= 1");
     return moe_b200::grouped_swiglu_impl(x_tokens, seg_start, seg_expert, nseg, rows, d, I, E, w_gate_up, w_down,
                                          dtype, h, y, static_cast<cudaStream_t>(stream), nullptr, nullptr, row_token,
-                                         T, nullptr);
+                                         T, nullptr, nullptr, 0);
 }

@@ -265,17 +265,22 @@ int moe_b200_ep_layout(const int32_t* all_counts, int nranks, int E, int rank,
  *                                 counts to every peer), then store every
  *                                 token row straight into the receive buffer
  *                                 of the rank owning its expert
- *   moe_b200_ep_receive           wait for all senders; segment table of the
- *                                 receive buffer, which is expert-major: one
- *                                 segment per local expert holding every
- *                                 sender's rows (seg_start L'+H+1 entries,
- *                                 seg_expert L'+H: L' = this rank's
- *                                 non-replicated experts, H = replicated ones)
- *   moe_b200_ep_ffn_return        grouped SwiGLU on the received rows whose
- *                                 down-GEMM stores every row straight into
- *                                 the sender's back buffer, at the return
- *                                 address the dispatch stored beside it
- *     or moe_b200_ep_return_identity   (identity expert)
+ *   moe_b200_ep_receive           wait for all senders' counts; segment
+ *                                 table of the receive buffer, which is
+ *                                 expert-major: one segment per local expert,
+ *                                 this rank's own rows of the H replicated
+ *                                 experts first, then the L' non-replicated
+ *                                 ones holding every sender's rows
+ *                                 (seg_start L'+H+1 entries, seg_expert L'+H)
+ *   moe_b200_ep_ffn_return        grouped SwiGLU on the received rows: the
+ *                                 gate/up GEMM starts on the replicated
+ *                                 segments and waits for the senders' rows
+ *                                 before the others; the down-GEMM stores
+ *                                 every row straight into the sender's back
+ *                                 buffer, at the return address the dispatch
+ *                                 stored beside it
+ *     or moe_b200_ep_return_identity   (identity expert; waits for the
+ *                                 senders' rows itself)
  *   moe_b200_ep_combine           wait for all returns; weighted unpermute
  * or all of it with one call, moe_b200_ep_step.
  * Replaces the reference's AllGather -> D2H -> host offsets -> grouped
