@@ -62,9 +62,10 @@ struct RouterHeader {
 };
 
 struct RouteSmem {
-    float merge_v[128][8];  // second half's top-K per token row
-    int merge_i[128][8];
-    float merge_f[128];     // row maximum, then the second half's partial sum
+    float merge_v[256][8];  // each epilogue thread's top-K over its expert range
+    int merge_i[256][8];
+    float merge_f[256];     // each epilogue thread's partial sum of exponentials
+    float row_max[128];
     uint64_t full[kRtMaxStages];
     uint64_t empty[kRtMaxStages];
     uint64_t done;
@@ -191,9 +192,11 @@ __device__ __forceinline__ void topk_insert(float (&bv)[K], int (&bi)[K], float 
 
 // One CTA per (128-token tile, K slice).  With nsplit > 1 the CTAs of a
 // tile form a cluster: each accumulates the logits of its slice of the d
-// input features in its own TMEM; the non-leader CTAs store their partial
-// logits into the leader's (by then idle) stage buffers over distributed
-// shared memory, and the leader's epilogue threads add them in rank order.
+// input features in its own TMEM, and CTA c finishes token rows
+// [c*R, c*R + R), R = 128 / nsplit: every CTA stores the partial logits of
+// each row into the (by then idle) stage buffers of the CTA that finishes
+// it, over distributed shared memory, and that CTA's epilogue threads add
+// the slices in rank order.
 template <int DT, int K>
 __global__ void __launch_bounds__(kRtThreads, 1)
 route_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
@@ -206,8 +209,8 @@ route_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__
     const uint32_t sbytes = stage_bytes(E_pad, P);
     const uint32_t piece_bytes = uint32_t(E_pad) * kRtTileK * 2;
     // stage buffers, then (over the same bytes, once the main loop is over)
-    // the logit rows: one per token and K slice, stride E_pad + 4 floats
-    // for conflict-free 16-byte accesses
+    // the logit rows of the R rows this CTA finishes, one per row and K
+    // slice, stride E_pad + 4 floats for conflict-free 16-byte accesses
     RouteSmem* ctl = reinterpret_cast<RouteSmem*>(base + area_bytes);
     float* s_logit = reinterpret_cast<float*>(base);
     const int lstride = E_pad + 4;
@@ -305,43 +308,51 @@ route_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__
             if (ok) umma_commit(&ctl->done);  // also when this slice is empty
         }
     }
-    // ---------------- epilogue warps 2-5: one token per thread ----------------
+    // ---------------- epilogue ----------------
     // Logit rows live over the (then idle) stage buffers: slot q holds the
-    // partial logits of K slice q, row r at slot q + r * lstride floats.
+    // partial logits of K slice q, finished-row j at slot q + j * lstride
+    // floats.
     const bool epi = warp >= 2;
     const bool copier = warp >= 2 && warp < 6;  // one warp per TMEM lane quadrant
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // token row within the tile = TMEM lane
-    const uint32_t t_row = tmem + (uint32_t(quad * 32) << 16);
-    const int slot_floats = kRtTileM * lstride;
+    const int R = kRtTileM / nsplit;  // rows this CTA finishes
+    const int slot_floats = R * lstride;
     bool have = false;
     if (copier && hdr_ok && wait_or_abort(&ctl->done, 0, abort_flag, dev_status)) {
         tc_fence_after();
         have = true;
     }
-    // A peer may write into the leader's stage buffers only once the
-    // leader's main loop is over: every CTA passes this barrier after its
-    // own accumulation completed.
+    // A peer may write into this CTA's stage buffers only once its main
+    // loop is over: every CTA passes this barrier after its own
+    // accumulation completed.
     if (nsplit > 1) rt_cluster_sync();
     if (have) {
-        // this CTA's partial logits -> slot crank of the leader (peers push
-        // over distributed shared memory; the leader writes locally)
-        float* dst_row = s_logit + int(crank) * slot_floats + r * lstride;
-        const uint32_t dst_cl = crank ? rt_mapa(smem_u32(dst_row), 0) : 0u;
+        // this CTA's partial logits of row r (= TMEM lane) -> slot crank of
+        // the CTA finishing r (peers over distributed shared memory, the
+        // own rows locally)
+        const int r = quad * 32 + lane;
+        const uint32_t dst_cta = uint32_t(r / R);
+        const uint32_t t_row = tmem + (uint32_t(quad * 32) << 16);
+        float* dst_row = s_logit + int(crank) * slot_floats + (r % R) * lstride;
+        const uint32_t dst_cl = dst_cta != crank ? rt_mapa(smem_u32(dst_row), dst_cta) : 0u;
         for (int c = 0; c < E_pad; c += 16) {
-            uint32_t v[16];
+            // every piece's columns in flight at once, one wait
+            uint32_t v[16], w[2][16];
             tmem_ld16(t_row + c, v);
-            tmem_wait_ld();
-            for (int p = 1; p < P; ++p) {  // hi + mid + lo pieces, in order
-                uint32_t w[16];
-                tmem_ld16(t_row + uint32_t(p * E_pad) + c, w);
-                tmem_wait_ld();
 #pragma unroll
-                for (int q = 0; q < 16; ++q) v[q] = __float_as_uint(__uint_as_float(v[q]) + __uint_as_float(w[q]));
+            for (int p = 1; p < 3; ++p)
+                if (p < P) tmem_ld16(t_row + uint32_t(p * E_pad) + c, w[p - 1]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int p = 1; p < 3; ++p) {  // hi + mid + lo pieces, in order
+                if (p >= P) break;
+#pragma unroll
+                for (int q = 0; q < 16; ++q)
+                    v[q] = __float_as_uint(__uint_as_float(v[q]) + __uint_as_float(w[p - 1][q]));
             }
 #pragma unroll
             for (int q = 0; q < 16; q += 4) {
-                if (crank == 0) {
+                if (dst_cta == crank) {
                     *reinterpret_cast<uint4*>(dst_row + c + q) = make_uint4(v[q], v[q + 1], v[q + 2], v[q + 3]);
                 } else {
                     asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst_cl + uint32_t(c + q) * 4u),
@@ -351,17 +362,21 @@ route_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__
             }
         }
     }
-    if (nsplit > 1) rt_cluster_sync();  // all partial rows are in the leader's slots
-    // The leader's softmax / top-K: two warps per token row (one per SM
-    // sub-partition pair), each over half of the experts, merged through
-    // shared memory -- twice the warps hide the latency of the serial
-    // per-row insertion chains.
-    if (epi && crank == 0) {
-        const int half = (warp - 2) >> 2;  // warps 2-5: experts [0, c_mid); warps 6-9: [c_mid, E)
-        const int c_mid = min(((E + 7) / 8) * 4, E);  // a multiple of 4 unless it is E
-        const int c_lo = half ? c_mid : 0, c_hi = half ? E : c_mid;
-        float* my_row = s_logit + r * lstride;
-        const bool work = have || half;  // the second half copied nothing itself
+    if (nsplit > 1) rt_cluster_sync();  // every slice of this CTA's rows is in its slots
+    // Softmax / top-K of the R rows: TPR = 256 / R threads per row (2, 4 or
+    // 8), each over a contiguous range of experts (a multiple of 4 but the
+    // last), merged through shared memory in ascending range order --
+    // several threads per row hide the latency of the serial insertion
+    // chains.
+    if (epi) {
+        const int et = threadIdx.x - 64;   // 0..255
+        const int j = et % R;              // finished row; consecutive lanes, consecutive rows
+        const int part = et / R;
+        const int tpr = 256 / R;
+        const int chunk = (((E + tpr - 1) / tpr) + 3) & ~3;
+        const int c_lo = min(part * chunk, E), c_hi = min(c_lo + chunk, E);
+        float* my_row = s_logit + j * lstride;
+        const bool work = hdr_ok && !*abort_flag;
         const float scale = ldexpf(1.0f, -hdr->scale_exp);
         if (nsplit == 1) named_bar_sync(1, 256);  // rows written by warps 2-5
         // pass 1: full logits (slices added in rank order), kept in slot 0,
@@ -394,28 +409,31 @@ route_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__
                     if (c + q < c_hi && lv[q] > bv[K - 1]) topk_insert<K>(bv, bi, lv[q], c + q);
             }
         }
-        if (half) {
+        if (part) {
 #pragma unroll
             for (int k = 0; k < K; ++k) {
-                ctl->merge_v[r][k] = bv[k];
-                ctl->merge_i[r][k] = bi[k];
+                ctl->merge_v[et][k] = bv[k];
+                ctl->merge_i[et][k] = bi[k];
             }
         }
         named_bar_sync(1, 256);
-        if (!half) {
-            // the second half's experts all follow the first half's, and
-            // its list is in the insertion order, so inserting it keeps ties
-            // ordered by index
+        if (!part) {
+            // each later range's experts all follow the earlier ones', and
+            // its list is in insertion order, so inserting the lists in
+            // range order keeps ties ordered by index
+            for (int pp = 1; pp < tpr; ++pp) {
+                const int src = pp * R + j;
 #pragma unroll
-            for (int k = 0; k < K; ++k) {
-                const float v = ctl->merge_v[r][k];
-                if (v > bv[K - 1]) topk_insert<K>(bv, bi, v, ctl->merge_i[r][k]);
+                for (int k = 0; k < K; ++k) {
+                    const float v = ctl->merge_v[src][k];
+                    if (v > bv[K - 1]) topk_insert<K>(bv, bi, v, ctl->merge_i[src][k]);
+                }
             }
-            ctl->merge_f[r] = bv[0];
+            ctl->row_max[j] = bv[0];
         }
         named_bar_sync(1, 256);
-        // pass 2: sum of exponentials, each half in ascending expert order
-        const float mx = ctl->merge_f[r];
+        // pass 2: sum of exponentials, each range in ascending expert order
+        const float mx = ctl->row_max[j];
         float sum = 0.f;
         if (work) {
             for (int c = c_lo; c < c_hi; c += 4) {
@@ -426,12 +444,12 @@ route_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__
                     if (c + q < c_hi) sum += e4[q];
             }
         }
-        named_bar_sync(1, 256);  // every thread has read the maximum
-        if (half) ctl->merge_f[r] = sum;
+        ctl->merge_f[et] = sum;
         named_bar_sync(1, 256);
-        const int t = row0 + r;
-        if (!half && have && t < T) {
-            sum += ctl->merge_f[r];
+        const int t = row0 + int(crank) * R + j;
+        if (!part && work && t < T) {
+            sum = 0.f;
+            for (int pp = 0; pp < tpr; ++pp) sum += ctl->merge_f[pp * R + j];
 #pragma unroll
             for (int k = 0; k < K; ++k) {
                 assignments[int64_t(t) * K + k] = bi[k];
@@ -554,13 +572,12 @@ extern "C" int moe_b200_route(const void* emb, int T, int d, int E, int K, int d
     const int tiles = (T + kRtTileM - 1) / kRtTileM;
     const int nk = (d + kRtTileK - 1) / kRtTileK;
     // Split the d features over a cluster of 2 or 4 CTAs per token tile when
-    // the tiles alone cannot fill the SMs (and the leader has room for every
-    // slice's logit rows).
+    // the tiles alone cannot fill the SMs.  Each CTA then finishes 128 /
+    // nsplit of the tile's rows and holds nsplit slices of them: 128 logit
+    // rows whatever nsplit.
     int nsplit = 1;
-    while (nsplit < 4 && tiles * nsplit * 2 <= sm_count_rt() && nsplit * 2 <= nk &&
-           slot_bytes * nsplit * 2 <= kRtStageBudget)
-        nsplit *= 2;
-    const size_t area = std::max(size_t(stages) * sb, slot_bytes * nsplit);
+    while (nsplit < 4 && tiles * nsplit * 2 <= sm_count_rt() && nsplit * 2 <= nk) nsplit *= 2;
+    const size_t area = std::max(size_t(stages) * sb, slot_bytes);
     if (area > kRtStageBudget)
         return fail(MOE_B200_ERR_UNSUPPORTED, "route: E=%d logit rows exceed shared memory", E);
     const size_t smem = 1024 + area + sizeof(RouteSmem);
