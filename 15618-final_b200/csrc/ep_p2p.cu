@@ -12,7 +12,8 @@
 //   back   [max_tokens * K][d] this rank's rows after their expert, in its
 //                              own packed order
 // One step (epoch e, the same on all ranks; epochs only grow, so no flag is
-// ever reset), five launches on one stream for the identity expert:
+// ever reset), on one stream: four launches for the identity expert, six for
+// the SwiGLU expert:
 //   1. route_scan (pack.cu): local counts / starts / ranks; the tile that
 //      finishes the scan writes the counts into every peer's inbox and raises
 //      counts flag = e on every peer (system-scope release)
@@ -20,12 +21,15 @@
 //      read once and stored K times straight into the receive buffer of the
 //      rank owning each slot's expert (NVLink stores); the last CTA raises
 //      data flag = e on every peer
-//   3. ep_receive_kernel (receiver): wait for all data flags, build the
-//      segment table of the receive buffer + each segment's return address
+//   3. ep_receive_kernel (receiver; the SwiGLU expert only): the segment
+//      table of the receive buffer.  Called alone (moe_b200_ep_receive) it
+//      first waits for all data flags, so any expert kernel may follow; in
+//      the one-call step it waits for the counts only and the gate/up GEMM
+//      waits for the data flags itself, after the replicated experts' rows
 //   4. the expert: grouped SwiGLU whose down-GEMM epilogue stores every row
 //      straight into the sender's back buffer (grouped_ffn.cu scatter mode),
-//      or ep_return_identity_kernel; the last CTA of either raises back
-//      flag = e on every peer
+//      or ep_return_identity_kernel (which waits for the data flags itself);
+//      the last CTA of either raises back flag = e on every peer
 //   5. unpermute (unpermute.cu): its copy warps wait for all back flags, then
 //      combine the local back buffer
 // Replicated ("hot") experts: every rank holds its own copy of the experts in
@@ -258,15 +262,17 @@ ep_pack_dispatch_kernel(EpGeom g, char* const* __restrict__ peer, const uint4* _
         ep_signal_done(EpSignal{peer, g.off_dflag, hdr->pad, g.rank, g.nranks, epoch}, s_fail != 0);
 }
 
-// Receiver: wait for every sender's counts (not its rows), then the segment
-// table of the receive buffer: one segment per local expert, the own rows of
-// the replicated experts first, then the range's non-replicated experts with
-// every sender's rows; seg_expert = the local expert index (local experts are
-// numbered non-replicated first, replicated last).  The kernels that read
-// the rows wait for the senders' data flags themselves.
+// Receiver: wait for every sender's rows (wait_rows) or only for its counts,
+// then the segment table of the receive buffer: one segment per local
+// expert, the own rows of the replicated experts first, then the range's
+// non-replicated experts with every sender's rows; seg_expert = the local
+// expert index (local experts are numbered non-replicated first, replicated
+// last).  Counts only: the kernels that read the rows wait for the senders'
+// data flags themselves.
 __global__ void __launch_bounds__(256)
 ep_receive_kernel(EpGeom g, char* const* __restrict__ peer, uint64_t epoch, int32_t* __restrict__ seg_start,
-                  int32_t* __restrict__ seg_expert, uint32_t* __restrict__ dev_status, int inbox_smem) {
+                  int32_t* __restrict__ seg_expert, uint32_t* __restrict__ dev_status, int inbox_smem,
+                  int wait_rows) {
     extern __shared__ int32_t s_inbox[];  // [N][E] when inbox_smem
     __shared__ int s_fail;
     __shared__ int32_t warp_tot[8];
@@ -277,8 +283,8 @@ ep_receive_kernel(EpGeom g, char* const* __restrict__ peer, uint64_t epoch, int3
     }
     __syncthreads();
     const char* mine = peer[g.rank];
-    wait_flags(reinterpret_cast<const uint64_t*>(mine + g.off_cflag), g.nranks, epoch, g.timeout_ns, dev_status,
-               &s_fail);
+    wait_flags(reinterpret_cast<const uint64_t*>(mine + (wait_rows ? g.off_dflag : g.off_cflag)), g.nranks, epoch,
+               g.timeout_ns, dev_status, &s_fail);
     const int32_t* inbox = reinterpret_cast<const int32_t*>(mine + g.off_inbox);
     if (inbox_smem) {
         for (int i = threadIdx.x; i < g.nranks * g.E; i += blockDim.x) s_inbox[i] = inbox[i];
@@ -636,13 +642,14 @@ static int ep_enqueue_dispatch(EpContext* ctx, uint64_t epoch, const void* emb, 
 }
 
 static int ep_enqueue_receive(EpContext* ctx, uint64_t epoch, int32_t* seg_start, int32_t* seg_expert,
-                              cudaStream_t s) {
+                              bool wait_rows, cudaStream_t s) {
     if (!seg_start || !seg_expert) return fail(MOE_B200_ERR_INVALID_ARG, "ep_receive: null segment buffer");
     uint32_t* st = device_status_word();
     if (!st) return fail(MOE_B200_ERR_CUDA, "ep_receive: device status word unavailable");
     const int inbox_smem = int64_t(ctx->g.nranks) * ctx->g.E <= kInboxSmemMax ? 1 : 0;
     const size_t smem = inbox_smem ? size_t(ctx->g.nranks) * ctx->g.E * 4 : 0;
-    ep_receive_kernel<<<1, 256, smem, s>>>(ctx->g, ctx->peer_dev, epoch, seg_start, seg_expert, st, inbox_smem);
+    ep_receive_kernel<<<1, 256, smem, s>>>(ctx->g, ctx->peer_dev, epoch, seg_start, seg_expert, st, inbox_smem,
+                                           wait_rows ? 1 : 0);
     cudaError_t err = cudaGetLastError();
     return err == cudaSuccess ? MOE_B200_OK : cuda_fail(err, "ep_receive launch");
 }
@@ -728,7 +735,8 @@ int moe_b200_ep_dispatch(void* c, uint64_t epoch, const void* emb, const int32_t
 int moe_b200_ep_receive(void* c, uint64_t epoch, int32_t* seg_start, int32_t* seg_expert, void* stream) {
     EpContext* ctx = connected_ctx(c, "ep_receive");
     if (!ctx) return MOE_B200_ERR_INVALID_ARG;
-    return ep_enqueue_receive(ctx, epoch, seg_start, seg_expert, static_cast<cudaStream_t>(stream));
+    // alone: the rows are in place when it ends, whatever expert follows
+    return ep_enqueue_receive(ctx, epoch, seg_start, seg_expert, true, static_cast<cudaStream_t>(stream));
 }
 
 int moe_b200_ep_return_identity(void* c, uint64_t epoch, const int32_t* seg_start, void* stream) {
@@ -773,7 +781,8 @@ int moe_b200_ep_step(void* c, const void* emb, const int32_t* asgn, const float*
                                  slot_pos, workspace, workspace_bytes, s);
     // identity: the return kernel waits for the senders itself (four launches
     // per step); the FFN needs the receive kernel's segment table
-    if (st == MOE_B200_OK && !identity) st = ep_enqueue_receive(ctx, epoch, seg_start, seg_expert, s);
+    // (the segment table from the counts; the gate/up GEMM waits for the rows)
+    if (st == MOE_B200_OK && !identity) st = ep_enqueue_receive(ctx, epoch, seg_start, seg_expert, false, s);
     if (st == MOE_B200_OK)
         st = identity ? ep_enqueue_return_identity(ctx, epoch, nullptr, s)
                       : ep_enqueue_ffn_return(ctx, epoch, seg_start, seg_expert, I, w_gate_up, w_down, dtype, h, s);

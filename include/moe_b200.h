@@ -265,13 +265,14 @@ int moe_b200_ep_layout(const int32_t* all_counts, int nranks, int E, int rank,
  *                                 counts to every peer), then store every
  *                                 token row straight into the receive buffer
  *                                 of the rank owning its expert
- *   moe_b200_ep_receive           wait for all senders' counts; segment
+ *   moe_b200_ep_receive           wait for all senders' rows; segment
  *                                 table of the receive buffer, which is
  *                                 expert-major: one segment per local expert,
  *                                 this rank's own rows of the H replicated
  *                                 experts first, then the L' non-replicated
  *                                 ones holding every sender's rows
- *                                 (seg_start L'+H+1 entries, seg_expert L'+H)
+ *                                 (seg_start L'+H+1 entries, seg_expert L'+H);
+ *                                 any expert kernel may read them after it
  *   moe_b200_ep_ffn_return        grouped SwiGLU on the received rows: the
  *                                 gate/up GEMM starts on the replicated
  *                                 segments and waits for the senders' rows
@@ -324,8 +325,9 @@ int moe_b200_ep_combine(void* ctx, uint64_t epoch, const float* packed_weights,
  * the next epoch (moe_b200_ep_epoch(ctx) + 1), four kernel launches for the
  * identity expert (w_gate_up = w_down = NULL; I and h unused; its return
  * kernel waits for the senders itself) and six for the grouped SwiGLU
- * (w_gate_up / w_down / h as moe_b200_ep_ffn_return).  The
- * segment table lives in the context.  Arguments otherwise as the stage
+ * (w_gate_up / w_down / h as moe_b200_ep_ffn_return; its receive waits for
+ * the counts only and the gate/up GEMM for the senders' rows, after the
+ * replicated experts' local rows).  The segment table lives in the context.  Arguments otherwise as the stage
  * calls; out [T, d] receives the combined rows.  Replaces one round of
  * apps/bench_prefill.cu:768-906 (count all-gather, host offsets, dispatch
  * AllToAllv, per-expert GEMMs, combine AllToAllv).                        */
