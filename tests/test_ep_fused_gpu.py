@@ -103,6 +103,11 @@ def test_fused_ep_single_rank_matches_single_gpu_layer(cuda, identity, replicate
         epx.close()
 
 
+def test_custom_expert_after_receive_single_rank(cuda):
+    assert _custom_expert_sees_rows(0, 1, torch.device("cuda", 0), 1024, 4, 12, 256, torch.bfloat16)
+    assert mb.device_status() == 0
+
+
 def test_fused_ep_wait_times_out_and_reports(cuda):
     """A flag nothing sets: the bounded wait gives up after the context's
     timeout, reports MOE_B200_DEV_WAIT_TIMEOUT, and the context stays usable."""
@@ -162,6 +167,50 @@ def _free_port():
     return p
 
 
+def _custom_expert_sees_rows(rank, world, dev, T, K, E, d, dtype):
+    """The stage calls with an expert kernel of the caller's own: right after
+    dispatch() and receive(), a torch kernel on the same stream (no host
+    synchronisation in between) sums every received row, masked on the device
+    by the segment table; the sum must equal the one computed from every
+    rank's inputs (regenerated here from their seeds): receive() has waited
+    for every sender's rows."""
+    replicated = (0, 1, 7)
+    epx = ep.FusedExpertParallel(E, K, d, T, dtype, device=dev, timeout_ms=5000, replicated=replicated)
+    try:
+        ws = mb.Workspace(T, K, E, device=dev)
+        out = mb.PackResult(packed=None,
+                            packed_weights=torch.empty(T * K, dtype=torch.float32, device=dev),
+                            perm=torch.empty(T * K, dtype=torch.int32, device=dev),
+                            expert_count=torch.empty(E, dtype=torch.int32, device=dev),
+                            expert_start=torch.empty(E + 1, dtype=torch.int32, device=dev),
+                            slot_pos=torch.empty(T * K, dtype=torch.int32, device=dev))
+        asgn, wts = routing.gen_routing(T, K, E, "zipf", seed=50 + rank)
+        x = routing.gen_rows(T, d, "bfloat16", seed=50 + rank, device=dev)
+        epx.dispatch(x, torch.from_numpy(asgn).to(dev), torch.from_numpy(wts).to(dev), ws, out)
+        epx.receive()
+        recv = epx.recv_rows()
+        live = torch.arange(recv.shape[0], device=dev) < epx.seg_start[-1]
+        got = (recv.double().sum(dim=1) * live).sum()
+        mine = set(epx.local_experts[:epx.L_range])
+        want = 0.0
+        for s in range(world):
+            a_s, _ = routing.gen_routing(T, K, E, "zipf", seed=50 + s)
+            rowsum = routing.gen_rows(T, d, "bfloat16", seed=50 + s, device=dev).double().sum(dim=1).cpu().numpy()
+            for t in range(T):
+                for e in a_s[t]:
+                    if int(e) in mine or (s == rank and int(e) in replicated):
+                        want += rowsum[t]
+        got = float(got.item())
+        # finish the step so that every rank's buffers are released in order
+        epx.return_identity()
+        y = torch.empty((T, d), dtype=dtype, device=dev)
+        epx.combine(out.packed_weights, out.slot_pos, T, y)
+        torch.cuda.synchronize(dev)
+        return abs(got - want) <= 1e-9 * max(1.0, abs(want))
+    finally:
+        epx.close()
+
+
 def _multi_worker(rank, world, port, results):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -193,6 +242,8 @@ def _multi_worker(rank, world, port, results):
                                                 for y in outs)
                 ok[("status",) + key] = mb.device_status()
                 epx.close()
+        ok["custom_expert"] = _custom_expert_sees_rows(rank, world, dev, T, K, E, d, dtype)
+        ok[("status", "custom")] = mb.device_status()
         results[rank] = ok
     finally:
         dist.barrier()
@@ -217,3 +268,5 @@ def test_fused_ep_multi_gpu_matches_single_gpu():
                 for one_call in (False, True):
                     assert res[r][(identity, nrep, one_call)], res
                 assert res[r][("status", identity, nrep)] == 0, res
+        assert res[r]["custom_expert"], res
+        assert res[r][("status", "custom")] == 0, res
